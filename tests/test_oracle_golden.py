@@ -1,0 +1,189 @@
+"""Pin the CPU oracle against golden vectors from the reference's own code.
+
+The fixtures were produced by tests/golden/make_golden.py from the X-MinimaxH3
+sources; each test names the reference function behind its fixture.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return np.load(os.path.join(G, name))
+
+
+def bf(b):
+    return O.bf16_bits_to_f32(b)
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def test_quant_rowwise_matches_eager_codes():
+    """comfy_kitchen eager quantize_int8_rowwise (eager/quantization.py:857-875)."""
+    z = load("quant_rowwise.npz")
+    q, s = O.quant_rowwise(z["x"])
+    np.testing.assert_array_equal(q, z["q"])
+    # CUDA kernel form absmax*(1/127) vs eager absmax/127: equal to within one fp32 ulp
+    np.testing.assert_allclose(s, z["scale"], rtol=2.5e-7, atol=0)
+
+
+def test_fht_matches_eager_rotation():
+    """ConvRot rotation vs eager _rotate_activation in fp32 (tensor/int8_utils.py:11-74)."""
+    z = load("convrot.npz")
+    rot = O.fht256(bf(z["x"]))
+    assert rel_l2(rot, z["rot_f32"]) < 1e-6
+    np.testing.assert_allclose(rot, z["rot_f32"], rtol=0, atol=2e-5 * np.abs(z["rot_f32"]).max())
+
+
+def test_convrot_codes_within_one_of_eager():
+    """Fused ConvRot quant vs eager quantize_and_rotate_rowwise (bf16 matmul rotation):
+    codes may differ by one (rarely two, where the eager bf16 scale moves) because
+    the eager rotation is a bf16 matmul while the CUDA kernel rotates in fp32."""
+    z = load("convrot.npz")
+    q, s = O.quant_rowwise_convrot(z["x"], 0)
+    diff = np.abs(q.astype(np.int32) - z["q_eager"].astype(np.int32))
+    assert diff.max() <= 2
+    assert (diff <= 1).mean() > 0.999
+    assert (diff == 0).mean() > 0.97
+    np.testing.assert_allclose(s, z["scale_eager"], rtol=1e-2)
+
+
+def test_input_activations_match_torch():
+    """gelu_tanh / swiglu (backends/_activations.py:41-53) to a few fp32 ulp."""
+    z = load("input_act.npz")
+    x = bf(z["x"])
+    # act applied inside the quantizer; check through the exported scalar functions
+    lib = O.lib()
+    gelu = np.vectorize(lambda v: 0.5 * v * (1.0 + lib.h3bo_tanhf(np.float32(0.7978845608028654 * (v + 0.044715 * v * v * v)))))(x.astype(np.float64))
+    np.testing.assert_allclose(gelu, z["gelu_f32"], rtol=2e-6, atol=2e-7)
+    K = x.shape[1] // 2
+    gate, up = x[:, :K].astype(np.float64), x[:, K:].astype(np.float64)
+    e = np.vectorize(lambda v: lib.h3bo_expf(np.float32(-v)))(gate)
+    sw = gate / (1.0 + e) * up
+    np.testing.assert_allclose(sw, z["swiglu_f32"], rtol=2e-6, atol=2e-7)
+
+
+def test_expf_accuracy():
+    lib = O.lib()
+    xs = np.concatenate([np.linspace(-100, 88, 20001), np.linspace(-1, 1, 5001)]).astype(np.float32)
+    ours = np.array([lib.h3bo_expf(float(v)) for v in xs], np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    ok = ref > 1.2e-38
+    rel = np.abs(ours[ok] - ref[ok]) / ref[ok]
+    assert rel.max() < 2.5e-7  # about two fp32 ulp
+
+
+@pytest.mark.parametrize("tag", ["g4_codebook_e4m3", "g16_uniform_f32", "g128_uniform_f32", "g16_codebook_e4m3"])
+def test_w4_decode_bit_exact(tag):
+    """eager _dequant_int4_grouped_to_int8 (eager/w4a8_int8.py:344-363)."""
+    z = load("w4_decode.npz")
+    cb = z[tag + "_codebook"]
+    out = O.w4_decode(z[tag + "_qdata"], z[tag + "_srel"], cb if cb.size else None, int(z[tag + "_G"]))
+    np.testing.assert_array_equal(out, z[tag + "_out"])
+
+
+def test_int8_linear_vs_eager_and_module():
+    """int8_linear: eager (eager/quantization.py:971-1062) and the ConvRotInt8Linear CPU
+    fallback (model/quantization.py:278-304), bf16 output within 1e-2 relative L2."""
+    z = load("linear.npz")
+    bias = bf(z["bias"])
+    out = O.int8_linear(z["x"], z["wq"], z["ws"], bias, convrot=0)
+    assert rel_l2(bf(out), bf(z["out_eager"])) < 1e-2
+    out_r = O.int8_linear(z["x"], z["wq"], z["ws"], bias, convrot=256)
+    assert rel_l2(bf(out_r), bf(z["out_eager_rot"])) < 1e-2
+    assert rel_l2(bf(out_r), bf(z["out_module_rot"])) < 2e-2
+
+
+def test_w4a8_linear_vs_eager_and_module():
+    """w4a8_int8_linear eager (eager/w4a8_int8.py:457-508) and ConvRotW4A8Linear CPU path."""
+    z = load("linear.npz")
+    wq = O.w4_decode(z["w4_qdata"], z["w4_srel"], None, int(z["w4_G"]))
+    out = O.int8_linear(z["x"], wq, z["w4_sch"], bf(z["bias"]), convrot=256)
+    assert rel_l2(bf(out), bf(z["out_w4_eager"])) < 1e-2
+    assert rel_l2(bf(out), bf(z["out_w4_module"])) < 2e-2
+
+
+def assert_pooled_equal(ours, ref):
+    """Pooled means are stored to bf16.  The Triton interpreter that produced the
+    fixture narrows fp32 to bf16 by truncation, where the GPU (and the oracle)
+    round to nearest even; so a fixture value may sit one bf16 step closer to
+    zero than ours, never anywhere else."""
+    a = O.bf16_bits_to_f32(ours).astype(np.float64)
+    b = O.bf16_bits_to_f32(ref).astype(np.float64)
+    d = np.abs(ours.astype(np.int64) - ref.astype(np.int64))
+    assert d.max() <= 1
+    m = d != 0
+    assert np.all(np.abs(b[m]) < np.abs(a[m]))
+    assert np.all(np.sign(a[m]) == np.sign(b[m]))
+
+
+def test_sparge_pool_sim_quant_reference_shapes():
+    """sparge_nhd.pool_sim_quant_nhd + hnd_compatible_key_mean_nhd (TRITON_INTERPRET)."""
+    z = load("sparge_pool.npz")
+    thr = np.full(4, -0.1, np.float32)
+    pq, sq, qq, qs = O.pool_sim_quant(z["q"], 128, thr)
+    assert_pooled_equal(pq, z["pq"])
+    np.testing.assert_array_equal(sq, z["sq"])
+    np.testing.assert_allclose(qs, z["qs"], rtol=1e-7)
+    L = z["q"].shape[0]
+    np.testing.assert_array_equal(qq[:, :L].transpose(1, 0, 2), z["qq"])
+    kmean = O.key_mean(z["k"])
+    np.testing.assert_array_equal(kmean, z["kmean"])
+    pk, sk, kq, ks = O.pool_sim_quant(z["k"], 64, thr, mean=kmean)
+    assert_pooled_equal(pk, z["pk"])
+    np.testing.assert_array_equal(sk, z["sk"])
+    np.testing.assert_allclose(ks, z["ks"], rtol=1e-7)
+    Lk = z["k"].shape[0]
+    np.testing.assert_array_equal(kq[:, :Lk].transpose(1, 0, 2), z["kq"])
+
+
+def test_sparge_similarity_thresholds():
+    z = load("sparge_pool.npz")
+    pb, sb, qb, sbs = O.pool_sim_quant(z["kb"], 64, z["thr2"])
+    np.testing.assert_array_equal(sb, z["sb"])
+    assert_pooled_equal(pb, z["pb"])
+    np.testing.assert_array_equal(qb.transpose(1, 0, 2), z["qb"])
+
+
+def test_lut_matches_reference_kernels():
+    """sparse_lut block_map_to_absolute_lut + absolute_lut_to_delta (TRITON_INTERPRET)."""
+    z = load("lut.npz")
+    bm = z["block_map"]
+    H, Qb, Kb = bm.shape
+    words = (Kb + 31) // 32
+    packed = np.zeros((H, Qb, words * 32), np.uint8)
+    packed[..., :Kb] = bm
+    bitmap = np.packbits(packed, axis=-1, bitorder="little").view(np.uint32)
+    lut, valid = O.bitmap_to_lut(bitmap, Kb)
+    np.testing.assert_array_equal(valid, z["valid"])
+    for h in range(H):
+        for i in range(Qb):
+            n = valid[h, i]
+            np.testing.assert_array_equal(lut[h, i, :n], z["lut"][h, i, :n])
+
+
+def test_fixed_topk_mask_matches_reference_selector():
+    """SplitModalityProtectedSpargeAttentionBackend.long_sequence_video_queries
+    (model/kernels.py:3668-3941) on tie-free integer inputs: block maps identical."""
+    z = load("mask_topk.npz")
+    thr = np.full(2, -0.1, np.float32)
+    pq, sq, _, _ = O.pool_sim_quant(z["q"], 128, thr)
+    pk, sk, _, _ = O.pool_sim_quant(z["k"], 64, thr)
+    np.testing.assert_array_equal(pk, z["pk"])
+    np.testing.assert_array_equal(sk, z["sk"])
+    Kb = pk.shape[1]
+    for topk in (50, 75):
+        for prot in (0, 100):
+            bm = O.block_mask(pq, sq, pk, sk, mode=0, budget=topk / 100.0, protected_kb=(prot + 63) // 64)
+            got = O.bitmap_to_bool(bm, Kb)
+            np.testing.assert_array_equal(got, z[f"topk{topk}_prot{prot}"], err_msg=f"topk{topk} prot{prot}")
