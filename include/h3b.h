@@ -1,0 +1,214 @@
+/*
+ * h3b.h -- C ABI of libh3b.so, the sm_100a (B200) kernels of the X-MinimaxH3
+ * DiT-block hot path: per-token INT8 activation quantization (optionally fused
+ * with RMSNorm + AdaLN and the ConvRot rotation), tcgen05 INT8 GEMMs with a
+ * fused dequant / bias / gated-residual epilogue, the W4A8 weight decode, and
+ * the SageAttention-style quantized attention with its Sparge block mask.
+ *
+ * Conventions (mirroring the comfy_kitchen launchers each entry replaces):
+ *  - plain pointers to device memory and int64 sizes; no framework types;
+ *  - the caller allocates every output and workspace; nothing here allocates
+ *    device memory;
+ *  - every launch is asynchronous on the caller's `stream` (a cudaStream_t,
+ *    0 = legacy default stream);
+ *  - every entry returns an int status: H3B_OK or a negative H3B_ERR_* code,
+ *    with a message for the calling thread in h3b_last_error().  Nothing
+ *    throws across this boundary (the reference launchers could, e.g.
+ *    comfy_kitchen backends/cuda/ops/int8_linear.cu:1311-1322).
+ *  - kernels that wait on hardware barriers give up after a bounded time and
+ *    record a code in a per-device status word read by h3b_device_status().
+ *  - dtype codes: 0 = float32, 1 = float16, 2 = bfloat16 (comfy_kitchen
+ *    backends/eager/quantization.py:34-42); bf16 is the only activation dtype
+ *    the kernels take.
+ * Head dimension is 128 throughout the attention entries (the reference's
+ * NHD Sparge helpers require it: model/sparge_nhd.py:176-177).
+ */
+#ifndef H3B_H_
+#define H3B_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3B_OK 0
+#define H3B_ERR_INVALID_ARGUMENT -1
+#define H3B_ERR_UNSUPPORTED -2
+#define H3B_ERR_CUDA -3
+#define H3B_ERR_NO_DEVICE -4
+/* device status codes (h3b_device_status) */
+#define H3B_STATUS_GEMM_TIMEOUT -101
+#define H3B_STATUS_ATTN_TIMEOUT -102
+
+/* ---------------------------------------------------------------- library */
+
+/* Version string of this build. */
+const char* h3b_version(void);
+
+/* Message describing the last failing call on this thread ("" if none). */
+const char* h3b_last_error(void);
+
+/* Reads the device status word of `device` (0 = no kernel has reported a
+ * problem) into *status; clears it when `reset` is non-zero.  Synchronizes
+ * the device. */
+int h3b_device_status(int device, int* status, int reset);
+
+/* ---------------------------------------------------------------- quantization */
+
+/* Per-row dynamic INT8 quantization: scale[r] = max(|x[r,:]|)/127 (at least
+ * 1e-30), q = rint(bf16(x / bf16(scale))) clamped to [-128, 127].
+ * x: bf16 [rows, x_row_stride] (first `cols` columns used), q: int8 [rows, cols],
+ * scales: f32 [rows].  cols % 16 == 0, cols <= 32768.
+ * Replaces launch_quantize_int8_rowwise_kernel
+ * (comfy_kitchen backends/cuda/ops/int8_linear.cu:1035-1084). */
+int h3b_quantize_int8_rowwise(const void* x, int64_t rows, int64_t cols, int64_t x_row_stride, void* q,
+                              void* scales, void* stream);
+
+/* Fused input activation + ConvRot (normalized regular-Hadamard rotation of
+ * every 256-column group, fp32) + per-row INT8 quantization.
+ * input_act: 0 none, 1 gelu_tanh, 2 swiglu (x row = [gate | up], 2*cols wide).
+ * x: bf16 [rows, x_row_stride]; q: int8 [rows, cols]; scales: f32 [rows].
+ * group_size must be 256; cols % 256 == 0, cols <= 32768.
+ * Replaces launch_quantize_int8_rowwise_convrot64 / _convrot_kernel
+ * (int8_linear.cu:1086-1160, 1294-1408). */
+int h3b_quantize_int8_rowwise_convrot(const void* x, int64_t rows, int64_t cols, int64_t x_row_stride,
+                                      int group_size, int input_act, void* q, void* scales, void* stream);
+
+/* RMSNorm(norm_weight, eps) + AdaLN modulation n*bf16(1+scale)+shift with the
+ * reference's bf16 materialization points, then (convrot_group_size 256) the
+ * ConvRot rotation or (0) nothing, then per-row INT8 quantization.
+ * x: bf16 [rows, cols] (row stride x_row_stride); norm_weight: bf16 [cols];
+ * scale_table / shift_table: bf16 [table_rows, cols]; segment_rows: int32
+ * [rows] giving each token's table row, or NULL for row 0.
+ * Replaces rms_adaln (model/kernels.py:7594-7642 -> backends/original/kernels/
+ * fused_norm_rope.py:12-45, 398-429) followed by the quantizer above. */
+int h3b_rms_adaln_quantize_int8(const void* x, int64_t rows, int64_t cols, int64_t x_row_stride,
+                                const void* norm_weight, const void* scale_table, const void* shift_table,
+                                const int32_t* segment_rows, float eps, int convrot_group_size, void* q,
+                                void* scales, void* stream);
+
+/* ---------------------------------------------------------------- GEMM */
+
+/* D[m, n] = bf16( float(sum_k A[m,k] * B[n,k]) * xs[m] * ws[n] + bias[n] ),
+ * int32 accumulation on tcgen05 (kind::i8) with TMEM accumulators.
+ * A: int8 [M, K] row-major; B: int8 [N, K] row-major (K-major weights);
+ * xs: f32 [M]; ws: f32 [N] or [1] (ws_numel 1 = scalar); bias: f32 [N] or NULL;
+ * D: bf16 with row stride out_row_stride (elements).  out_dtype must be 2.
+ * K % 16 == 0; A, B 16-byte aligned.
+ * Replaces launch_cutlass_int8_dequant / _strided
+ * (comfy_kitchen backends/cuda/ops/cutlass_gemm_int8.cu:612-666). */
+int h3b_int8_gemm_dequant(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,
+                          const void* bias, void* D, int64_t M, int64_t N, int64_t K, int64_t out_row_stride,
+                          int out_dtype, void* stream);
+
+/* As h3b_int8_gemm_dequant, but the bf16 result y[m,n] is added into a bf16
+ * residual stream in place: residual[m,n] = bf16(residual + y * gate[n])
+ * (gate: bf16 [N]).  Replaces int8_linear followed by residual.addcmul_
+ * (model/fused_mlp.py:393-425; model/layers.py:944-960). */
+int h3b_int8_gemm_gated_residual(const void* A, const void* B, const void* xs, const void* ws,
+                                 int64_t ws_numel, const void* bias, const void* gate, void* residual,
+                                 int64_t M, int64_t N, int64_t K, int64_t residual_row_stride, void* stream);
+
+/* Raw int32 accumulators acc[m, n] = sum_k A[m,k] * B[n,k] (same tcgen05
+ * pipeline), for bit-exact verification.  acc: int32 [M, N]. */
+int h3b_int8_gemm_i32(const void* A, const void* B, void* acc, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---------------------------------------------------------------- W4A8 */
+
+/* Grouped packed-int4 -> int8 grid: out[n,k] = clamp(rint(level * s_rel[n, k/G]), +-127)
+ * with level = codebook[c] or c - 8, c the nibble (even column = low nibble).
+ * qweight: int8 [N, K/2]; s_rel: [N, K/G] f32 (s_rel_kind 0) or e4m3 bytes (1);
+ * codebook: f32 [16] or NULL; out: int8 [N, K].  G in {4, 8, 16, 32, ...}, K % 32 == 0.
+ * Replaces launch_dequant_int4_grouped_to_int8(_e4m3)
+ * (comfy_kitchen backends/cuda/ops/w4a8_gemm.cu:94-123). */
+int h3b_dequant_int4_grouped_to_int8(const void* qweight, const void* s_rel, int s_rel_kind,
+                                     const void* codebook, void* out, int64_t N, int64_t K, int64_t G,
+                                     void* stream);
+
+/* ---------------------------------------------------------------- attention preparation */
+
+/* Bytes of workspace h3b_key_mean needs for L tokens and H heads. */
+int64_t h3b_key_mean_workspace_bytes(int64_t L, int64_t H);
+
+/* Per-(head, channel) mean of K over all L tokens (double accumulation, fixed
+ * order: 1024-token chunks, then chunk sums), rounded to bf16.
+ * k: bf16 NHD rows [L, H*128] with row stride k_row_stride; mean: bf16 [H, 128].
+ * Replaces hnd_compatible_key_mean_nhd (model/sparge_nhd.py:26-48). */
+int h3b_key_mean(const void* k, int64_t L, int64_t H, int64_t k_row_stride, void* mean, void* workspace,
+                 int64_t workspace_bytes, void* stream);
+
+/* Sparge per-block preparation of Q (block 128) or K (block 64, with `mean`
+ * for K mean-smoothing value = bf16(x - mean)):
+ *   pooled  bf16 [H, nb, 128]  = bf16(sum(value)/valid_rows)
+ *   similar u8   [H, nb]       = mean cosine Gram of fp16-normalised rows > thr[h]
+ *   qi8     int8 [H, Lpad, 128] = trunc(value/s + 0.5*sign(value/s)), padded rows 0
+ *   scale   f32  [H, nb]       = max|value| / 127 + 1e-7
+ * x: bf16 NHD [L, H*128] rows of stride x_row_stride; nb = ceil(L/block),
+ * Lpad >= nb*block (rows beyond nb*block are not written); thr: f32 [H].
+ * Replaces pool_sim_quant_nhd (model/sparge_nhd.py:51-227). */
+int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride, const void* mean,
+                       int block, const void* thr, void* pooled, void* similar, void* qi8, void* scale,
+                       int64_t Lpad, void* stream);
+
+/* V -> FP8 E4M3 per-(head, channel) scaled by 2.25/absmax, transposed to
+ * vt [H, 128, Lpad] (token index innermost, rows >= L zero); vscale: f32
+ * [H, 128] = absmax/2.25.  v: bf16 NHD [L, H*128], row stride v_row_stride.
+ * Lpad % 128 == 0.  Replaces prepare_sage_fp8_hnd_direct / write_sage_fp8_slab
+ * (model/compact_fp8.py:205-300); the sm89 16-row MMA permutation is not applied. */
+int h3b_value_fp8(const void* v, int64_t L, int64_t H, int64_t v_row_stride, int64_t Lpad, void* vt,
+                  void* vscale, void* stream);
+
+/* ---------------------------------------------------------------- block-sparse mask */
+
+/* Parameters of the block-sparse selector (model/kernels.py:3668-3941). */
+typedef struct h3b_mask_params {
+  int mode;                     /* 0 fixed Top-K: count = (int64)(budget[h]*Kb)
+                                   1 top-CDF: smallest-rank prefix with cumulative
+                                     probability <= budget[h] */
+  const float* budget;          /* host or device? -> device f32 [H] */
+  int64_t protected_key_blocks; /* first blocks always kept (protected prefix) */
+  int keep_first_column;        /* always keep K block 0 */
+  int keep_diagonal;            /* always keep K blocks 2i, 2i+1 for Q block i */
+  int temporal_radius;          /* < 0 off; else the temporal correspondence rail */
+  int temporal_spatial_radius;
+  int64_t frames, frame_tokens, protected_tokens, query_tokens;
+} h3b_mask_params;
+
+/* Pooled scores softmax(bf16(pq . pk) * 128^-0.5, non-similar K -> -inf) per
+ * (head, Q block), selection, and the mandatory rails (non-similar K columns
+ * and Q rows kept dense).  pooled_q: bf16 [H, Qb, 128], similar_q: u8 [H, Qb],
+ * pooled_k: bf16 [H, Kb, 128], similar_k: u8 [H, Kb].  Output bitmap: uint32
+ * [H, Qb, ceil(Kb/32)], bit j%32 of word j/32 set when K block j is kept.
+ * Kb <= 8192. */
+int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, const void* pooled_k,
+                   const void* similar_k, int64_t Kb, int64_t H, const h3b_mask_params* params, void* bitmap,
+                   void* stream);
+
+/* Bitmap -> the Sparge delta-LUT ABI: lut int32 [rows, Kb] (first entry absolute,
+ * then deltas; unused tail zero), valid int32 [rows].
+ * Replaces parallel_block_map_lut (model/sparse_lut.py:144-192). */
+int h3b_bitmap_to_lut(const void* bitmap, int64_t rows, int64_t Kb, void* lut, void* valid, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/* O = softmax(Q K^T * sm_scale) V with INT8 Q.K^T (tcgen05 kind::i8), fp32
+ * online softmax, P and V in FP8 E4M3 (tcgen05 kind::f8f6f4), fp32 output
+ * accumulation.  Visits only the K blocks whose bit is set in `bitmap`
+ * ([H, ceil(Lq/128), ceil(Kb/32)] words) or all of them when bitmap is NULL.
+ * q: int8 [H, Lqpad, 128], q_scale f32 [H, ceil(Lq/q_block)] (q_block 64 or 128);
+ * k: int8 [H, Lkpad, 128], k_scale f32 [H, ceil(Lk/64)];
+ * vt: e4m3 [H, 128, Lkpad], v_scale f32 [H, 128];
+ * out: bf16 NHD rows [Lq, H*128] with row stride out_row_stride.
+ * Lqpad % 128 == 0, Lkpad % 128 == 0.
+ * Replaces sageattn qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf and the
+ * Sparge block-sparse variant (model/kernels.py:7645-7661, 3981-3997). */
+int h3b_attention(const void* q, const void* q_scale, int q_block, int64_t Lq, int64_t Lqpad, const void* k,
+                  const void* k_scale, int64_t Lk, int64_t Lkpad, const void* vt, const void* v_scale, int64_t H,
+                  const void* bitmap, float sm_scale, void* out, int64_t out_row_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H_ */

@@ -246,24 +246,19 @@ void h3bo_quant_rowwise_convrot(const uint16_t* x, int64_t M, int64_t K, int act
     free(row);
 }
 
-/* RMSNorm(weight) followed by AdaLN modulation with bf16 materialization after
- * each step (fused_norm_rope.py:12-45; layers.py:916-941):
- *   n = bf16(x * inv_rms * w); n = bf16(n * bf16(1 + scale)); n = bf16(n + bf16(shift)).
- * inv_rms = 1 / sqrt(mean(x^2) + eps).  The sum of squares follows the CUDA
- * kernel's fixed order: thread t of `nthreads` sums columns t*8 .. t*8+7 of each
- * 8*nthreads-wide chunk in order, then the per-thread sums are combined by
- * block_tree_sum (nthreads a multiple of 32, nthreads/32 a power of two). */
 static float tree_sum(float* v, int n) {   /* n is a power of two; v is clobbered */
     for (int w = n / 2; w >= 1; w /= 2)
         for (int i = 0; i < w; ++i) v[i] = v[i] + v[i + w];
     return v[0];
 }
 /* Block reduction as the CUDA kernels do it: a shfl_down tree inside each warp
- * of 32 (pairs i, i+w for w = 16..1), then the same tree over the warp sums. */
+ * of 32 (pairs i, i+w for w = 16..1), then the same tree over the warp sums
+ * zero-padded to 32 entries.  n is a multiple of 32, at most 1024. */
 static float block_tree_sum(float* v, int n) {
     int nw = n / 32;
-    for (int w = 0; w < nw; ++w) v[w] = tree_sum(v + 32 * w, 32);
-    return tree_sum(v, nw);
+    float ws[32];
+    for (int w = 0; w < 32; ++w) ws[w] = w < nw ? tree_sum(v + 32 * w, 32) : 0.0f;
+    return tree_sum(ws, 32);
 }
 float h3bo_tree_sum(const float* v, int n) {
     float* t = (float*)malloc(sizeof(float) * (size_t)n);
@@ -273,16 +268,33 @@ float h3bo_tree_sum(const float* v, int n) {
     return r;
 }
 
+/* Threads per row used by the CUDA quantizer: K/16 chunks of 16 columns,
+ * rounded up to a warp multiple, at most 1024 (thread t owns chunks t, t+T, ...). */
+int h3bo_quant_threads(int64_t K) {
+    int64_t chunks = K / 16;
+    int64_t T = (chunks + 31) / 32 * 32;
+    return (int)(T > 1024 ? 1024 : T);
+}
+
+/* RMSNorm(weight) followed by AdaLN modulation with bf16 materialization after
+ * each step (fused_norm_rope.py:12-45; layers.py:916-941):
+ *   n = bf16(x * inv_rms * w); n = bf16(n * bf16(1 + scale)); n = bf16(n + bf16(shift)).
+ * inv_rms = 1 / sqrt(sum(x^2)/K + eps).  The sum of squares follows the CUDA
+ * kernel's fixed order: thread t of T = h3bo_quant_threads(K) adds the squares
+ * of its chunks t, t+T, ... (16 columns each, in column order), then the
+ * per-thread sums are combined by block_tree_sum. */
 void h3bo_rms_adaln_row(const uint16_t* xr, int64_t K, const uint16_t* w, const uint16_t* scale,
-                        const uint16_t* shift, float eps, int nthreads, float* out) {
-    float* part = (float*)calloc((size_t)nthreads, sizeof(float));
-    for (int64_t c0 = 0; c0 < K; c0 += 8 * (int64_t)nthreads)
-        for (int t = 0; t < nthreads; ++t)
-            for (int j = 0; j < 8; ++j) {
-                int64_t c = c0 + (int64_t)t * 8 + j;
-                if (c < K) { float v = bf16_to_f32(xr[c]); part[t] = part[t] + v * v; }
+                        const uint16_t* shift, float eps, float* out) {
+    int T = h3bo_quant_threads(K);
+    int64_t chunks = K / 16;
+    float* part = (float*)calloc(1024, sizeof(float));
+    for (int t = 0; t < T; ++t)
+        for (int64_t c = t; c < chunks; c += T)
+            for (int j = 0; j < 16; ++j) {
+                float v = bf16_to_f32(xr[c * 16 + j]);
+                part[t] = part[t] + v * v;
             }
-    float ss = block_tree_sum(part, nthreads);
+    float ss = block_tree_sum(part, T);
     free(part);
     float inv = 1.0f / sqrtf(ss / (float)K + eps);
     for (int64_t c = 0; c < K; ++c) {
@@ -301,12 +313,12 @@ void h3bo_rms_adaln_row(const uint16_t* xr, int64_t K, const uint16_t* w, const 
  * each token (segments of layers.py:916-941). */
 void h3bo_rms_adaln_quant(const uint16_t* x, int64_t M, int64_t K, const uint16_t* w,
                           const uint16_t* scale_tab, const uint16_t* shift_tab, const int32_t* seg_row,
-                          float eps, int nthreads, int convrot, int8_t* q, float* scales) {
+                          float eps, int convrot, int8_t* q, float* scales) {
     float* row = (float*)malloc(sizeof(float) * (size_t)K);
     for (int64_t m = 0; m < M; ++m) {
         int r = seg_row ? seg_row[m] : 0;
         h3bo_rms_adaln_row(x + m * K, K, w, scale_tab + (int64_t)r * K, shift_tab + (int64_t)r * K,
-                           eps, nthreads, row);
+                           eps, row);
         float amax = 0.0f;
         if (convrot)
             for (int64_t g = 0; g < K; g += 256) h3bo_fht256(row + g);
@@ -383,14 +395,22 @@ void h3bo_epilogue(const int32_t* acc, int64_t M, int64_t N, const float* xs, co
 /* ------------------------------------------------------------------------- */
 
 /* Per-(head, channel) mean of K over all L tokens, NHD bf16 input [L,H,D].
- * Accumulated in double (exact for bf16 inputs within a 2^53 dynamic range, so
- * independent of order), divided by L, rounded to float then bf16. */
+ * Accumulated in double in the CUDA kernels' order: the sum of each chunk of
+ * 1024 consecutive tokens (tokens in order), then the chunk sums in chunk
+ * order; divided by L, rounded to float, then to bf16.  For bf16 inputs the
+ * double sums are exact in practice, so the order matters only formally. */
+#define H3B_KEY_MEAN_CHUNK 1024
 void h3bo_key_mean(const uint16_t* k, int64_t L, int64_t H, int64_t D, uint16_t* mean) {
     for (int64_t h = 0; h < H; ++h)
         for (int64_t d = 0; d < D; ++d) {
-            double s = 0.0;
-            for (int64_t l = 0; l < L; ++l) s += (double)bf16_to_f32(k[(l * H + h) * D + d]);
-            mean[h * D + d] = f32_to_bf16((float)(s / (double)L));
+            double total = 0.0;
+            for (int64_t c0 = 0; c0 < L; c0 += H3B_KEY_MEAN_CHUNK) {
+                double part = 0.0;
+                int64_t c1 = c0 + H3B_KEY_MEAN_CHUNK < L ? c0 + H3B_KEY_MEAN_CHUNK : L;
+                for (int64_t l = c0; l < c1; ++l) part += (double)bf16_to_f32(k[(l * H + h) * D + d]);
+                total += part;
+            }
+            mean[h * D + d] = f32_to_bf16((float)(total / (double)L));
         }
 }
 
@@ -441,25 +461,31 @@ void h3bo_pool_sim_quant(const uint16_t* x, int64_t L, int64_t H, const uint16_t
                     }
                     v[r * D + d] = val;
                 }
-            /* pooled */
-            for (int d = 0; d < D; ++d) {
-                float s = 0.0f;
-                for (int r = 0; r < valid; ++r) s = s + v[r * D + d];
-                pooled[(h * nb + b) * D + d] = f32_to_bf16(s / (float)valid);
-            }
-            /* similarity */
-            float ssum[128];
-            for (int d = 0; d < D; ++d) ssum[d] = 0.0f;
+            /* The CUDA kernel runs four warps per block; warp w takes rows w, w+4, ...
+             * in order and the four partial sums are combined as (p0+p2)+(p1+p3). */
+            float pp[4][128], sp[4][128];
+            memset(pp, 0, sizeof(pp));
+            memset(sp, 0, sizeof(sp));
             int nan_seen = valid < blk;
             for (int r = 0; r < valid; ++r) {
+                int w = r & 3;
                 float sq[128];
-                for (int d = 0; d < D; ++d) sq[d] = v[r * D + d] * v[r * D + d];
+                for (int d = 0; d < D; ++d) {
+                    pp[w][d] = pp[w][d] + v[r * D + d];
+                    sq[d] = v[r * D + d] * v[r * D + d];
+                }
                 float norm = sqrtf(warp_sum128(sq));
                 if (!(norm > 0.0f)) nan_seen = 1;
                 for (int d = 0; d < D; ++d) {
                     float nv = f16_to_f32(f32_to_f16(v[r * D + d] / norm));
-                    ssum[d] = ssum[d] + nv;
+                    sp[w][d] = sp[w][d] + nv;
                 }
+            }
+            float ssum[128];
+            for (int d = 0; d < D; ++d) {
+                float s = (pp[0][d] + pp[2][d]) + (pp[1][d] + pp[3][d]);
+                pooled[(h * nb + b) * D + d] = f32_to_bf16(s / (float)valid);
+                ssum[d] = (sp[0][d] + sp[2][d]) + (sp[1][d] + sp[3][d]);
             }
             float sq2[128];
             for (int d = 0; d < D; ++d) sq2[d] = ssum[d] * ssum[d];
@@ -553,8 +579,9 @@ static int cmp_desc_idx(const void* a, const void* b) {
 }
 
 /* mode 0: fixed Top-K, count = (int64)(topk[h] * Kb) (kernels.py:3206-3253)
- * mode 1: top-CDF, count = #{r : cdf_r <= cdf_thr[h]} with cdf over the sorted
- *         probabilities summed in rank order in fp32 (SpargeAttn meansim rule)
+ * mode 1: top-CDF, count = #{r : cdf_r <= cdf_thr[h]} with cdf_r the sum of the
+ *         sorted probabilities of ranks 0..r (SpargeAttn meansim rule), summed
+ *         exactly in 2^-56 fixed point so any summation order gives the same count
  * rails (always): non-similar K column, non-similar Q row, the first
  *   `protected_kb` columns; optional (flags bit0) column 0, (bit1) the diagonal
  *   K blocks covering the Q block's rows; (temporal_radius >= 0) the temporal
@@ -583,10 +610,12 @@ void h3bo_block_mask(const uint16_t* pooled_q, const uint8_t* simq, int64_t Qb, 
                 if (mode == 0) {
                     count = (int64_t)(budget[h] * (float)Kb);
                 } else {
-                    float cdf = 0.0f; count = 0;
+                    /* cumulative probability in exact 2^-56 fixed point */
+                    uint64_t thr_fx = (uint64_t)(budget[h] * 72057594037927936.0f);
+                    uint64_t cdf = 0; count = 0;
                     for (int64_t r = 0; r < Kb; ++r) {
-                        cdf = cdf + bf16_to_f32((uint16_t)(keys[r] >> 16));
-                        if (cdf <= budget[h]) count = r + 1; else break;
+                        cdf += (uint64_t)(bf16_to_f32((uint16_t)(keys[r] >> 16)) * 72057594037927936.0f);
+                        if (cdf <= thr_fx) count = r + 1; else break;
                     }
                 }
                 if (count > Kb) count = Kb;

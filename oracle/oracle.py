@@ -108,7 +108,7 @@ def fht256(v: np.ndarray) -> np.ndarray:
 
 
 def rms_adaln_quant(x_bf16, w_bf16, scale_tab_bf16, shift_tab_bf16, seg_row=None, eps=1e-5,
-                    nthreads=256, convrot=True):
+                    convrot=True):
     x = _c(x_bf16, np.uint16)
     M, K = x.shape
     w = _c(w_bf16, np.uint16)
@@ -118,7 +118,7 @@ def rms_adaln_quant(x_bf16, w_bf16, scale_tab_bf16, shift_tab_bf16, seg_row=None
     q = np.empty((M, K), np.int8)
     s = np.empty((M,), np.float32)
     lib().h3bo_rms_adaln_quant(_p(x), I64(M), I64(K), _p(w), _p(sc), _p(sh), _p(sr),
-                               ctypes.c_float(eps), ctypes.c_int(nthreads), ctypes.c_int(int(convrot)),
+                               ctypes.c_float(eps), ctypes.c_int(int(convrot)),
                                _p(q), _p(s))
     return q, s
 

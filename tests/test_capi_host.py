@@ -1,0 +1,92 @@
+"""CPU-side checks of the C ABI library and the host logic (no GPU needed).
+
+The library must load, export every entry point include/h3b.h declares, and
+reject bad arguments with a status code and message before touching CUDA.
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import h3b
+from h3b import ops
+from h3b._lib import EXPORTED, lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "h3b.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(h3b_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    declared = header_symbols()
+    assert declared, "no declarations parsed"
+    handle = ctypes.CDLL(h3b.LIB_PATH)
+    for name in declared:
+        assert hasattr(handle, name), f"{name} declared in include/h3b.h but not exported"
+    assert set(declared) == set(EXPORTED), "ctypes signature table and header disagree"
+
+
+def test_version_and_error_string():
+    assert lib().h3b_version().startswith(b"h3b")
+    assert lib().h3b_last_error() is not None
+
+
+def test_null_pointer_is_rejected_without_cuda():
+    st = lib().h3b_quantize_int8_rowwise(None, 4, 256, 256, None, None, None)
+    assert st == -1
+    assert b"null" in lib().h3b_last_error()
+
+
+def test_unsupported_shapes_are_rejected():
+    dummy = ctypes.c_void_p(16)
+    assert lib().h3b_quantize_int8_rowwise_convrot(dummy, 4, 300, 300, 256, 0, dummy, dummy, None) == -2
+    assert lib().h3b_quantize_int8_rowwise_convrot(dummy, 4, 256, 256, 128, 0, dummy, dummy, None) == -2
+    assert lib().h3b_quantize_int8_rowwise_convrot(dummy, 4, 256, 256, 256, 7, dummy, dummy, None) == -1
+    assert lib().h3b_int8_gemm_dequant(dummy, dummy, dummy, dummy, 1, None, dummy, 8, 8, 24, 8, 2, None) == -2
+    assert lib().h3b_int8_gemm_dequant(dummy, dummy, dummy, dummy, 1, None, dummy, 8, 8, 32, 8, 0, None) == -2
+    assert lib().h3b_dequant_int4_grouped_to_int8(dummy, dummy, 0, None, dummy, 8, 64, 3, None) == -2
+    assert lib().h3b_attention(dummy, dummy, 96, 10, 128, dummy, dummy, 10, 128, dummy, dummy, 1, None,
+                               0.1, dummy, 128, None) == -2
+
+
+def test_empty_inputs_are_no_ops():
+    assert lib().h3b_quantize_int8_rowwise(None, 0, 256, 256, None, None, None) == 0
+    assert lib().h3b_int8_gemm_dequant(None, None, ctypes.c_void_p(16), ctypes.c_void_p(16), 1, None,
+                                       ctypes.c_void_p(16), 0, 8, 32, 8, 2, None) == 0
+
+
+def test_key_mean_workspace_size():
+    # one fp64 partial sum per (1024-token chunk, head, channel)
+    assert lib().h3b_key_mean_workspace_bytes(111600, 32) == 109 * 32 * 128 * 8
+
+
+def test_ops_refuse_cpu_tensors():
+    x = torch.zeros(4, 256, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.quantize_int8_rowwise(x)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.int8_linear(x, torch.zeros(8, 256, dtype=torch.int8), torch.ones(8))
+
+
+def test_segment_rows():
+    assert ops.segment_rows(None, 10, "cpu") is None
+    assert ops.segment_rows(((0, 10, 0),), 10, "cpu") is None
+    seg = ops.segment_rows(((0, 3, 1), (3, 10, 2)), 10, "cpu")
+    assert seg.tolist() == [1, 1, 1, 2, 2, 2, 2, 2, 2, 2]
+    with pytest.raises(ValueError):
+        ops.segment_rows(((0, 3, 1), (4, 10, 2)), 10, "cpu")
+    with pytest.raises(ValueError):
+        ops.segment_rows(((0, 9, 1),), 10, "cpu")
+
+
+def test_act_code_validation():
+    assert ops.act_code(None) == 0 and ops.act_code("gelu_tanh") == 1 and ops.act_code("swiglu") == 2
+    with pytest.raises(ValueError, match="unsupported input_act"):
+        ops.act_code("relu")

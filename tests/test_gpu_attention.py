@@ -1,0 +1,206 @@
+"""GPU parity of the attention preparation, the Sparge mask and the tcgen05
+quantized attention kernel.
+
+Preparation (K mean, pool / similarity / INT8, V FP8), the block mask and the
+LUT are bit-exact against the CPU oracle; the attention output meets
+cos >= 0.999 and rel-L2 <= 2e-2 against the oracle's exact-softmax attention
+over the same quantized operands, and stays close to fp32 attention on the
+unquantized inputs.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import bits, cosine, from_bits, rel_l2
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def attn():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from h3b import attention as _attn
+    return _attn
+
+
+def qkv(L, H, seed, k_offset=True, Lk=None):
+    g = torch.Generator().manual_seed(seed)
+    Lk = Lk or L
+    q = torch.randn(L, H, 128, generator=g)
+    k = torch.randn(Lk, H, 128, generator=g)
+    if k_offset:
+        k = k + torch.randn(1, H, 128, generator=g) * 3.0   # per-channel offset
+    v = torch.randn(Lk, H, 128, generator=g)
+    return q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("L,H", [(197, 4), (1000, 2), (4096, 1)])
+def test_key_mean_bit_exact(attn, L, H):
+    _, k, _ = qkv(L, H, seed=L)
+    m = attn.key_mean(k.cuda())
+    np.testing.assert_array_equal(bits(m), O.key_mean(bits(k)))
+
+
+@pytest.mark.parametrize("block", [64, 128])
+@pytest.mark.parametrize("L,H,smooth", [(131, 4, False), (197, 4, True), (1000, 3, True), (64, 1, False)])
+def test_pool_sim_quant_bit_exact(attn, block, L, H, smooth):
+    _, k, _ = qkv(L, H, seed=L + block)
+    kc = k.cuda()
+    mean = attn.key_mean(kc) if smooth else None
+    pb = attn.prepare_blocks(kc, block, -0.1, mean)
+    po, so, qo, sco = O.pool_sim_quant(bits(k), block, np.full(H, -0.1, np.float32),
+                                       None if mean is None else bits(mean))
+    np.testing.assert_array_equal(bits(pb.pooled), po)
+    np.testing.assert_array_equal(pb.similar.cpu().numpy(), so)
+    np.testing.assert_array_equal(pb.scale.cpu().numpy(), sco)
+    nb = po.shape[1]
+    np.testing.assert_array_equal(pb.qi8[:, :nb * block].cpu().numpy(), qo)
+
+
+def test_pool_sim_quant_reference_golden(attn):
+    """The reference's pool_sim_quant_nhd fixture (seed 82736, Lq=131, Lk=197, H=4)."""
+    z = np.load(os.path.join(G, "sparge_pool.npz"))
+    q = from_bits(z["q"])
+    pq = attn.prepare_blocks(q, 128, -0.1)
+    np.testing.assert_array_equal(pq.similar.cpu().numpy(), z["sq"])
+    np.testing.assert_array_equal(pq.qi8[:, :131].permute(1, 0, 2).cpu().numpy(), z["qq"])
+    k = from_bits(z["k"])
+    mean = attn.key_mean(k)
+    np.testing.assert_array_equal(bits(mean), z["kmean"])
+    pk = attn.prepare_blocks(k, 64, -0.1, mean)
+    np.testing.assert_array_equal(pk.similar.cpu().numpy(), z["sk"])
+    np.testing.assert_array_equal(pk.qi8[:, :197].permute(1, 0, 2).cpu().numpy(), z["kq"])
+
+
+@pytest.mark.parametrize("L,H", [(997, 4), (128, 2), (1, 1)])
+def test_value_fp8_bit_exact(attn, L, H):
+    _, _, v = qkv(L, H, seed=L * 3)
+    pv = attn.prepare_values(v.cuda())
+    vt, vs = O.value_fp8(bits(v), pv.padded)
+    np.testing.assert_array_equal(pv.vt.cpu().numpy(), vt)
+    np.testing.assert_array_equal(pv.scale.cpu().numpy(), vs)
+
+
+def _prepared_pair(attn, L, H, seed, Lk=None):
+    q, k, v = qkv(L, H, seed, Lk=Lk)
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    pk, mean = attn.prepare_keys(kc)
+    pq = attn.prepare_queries(qc)
+    pv = attn.prepare_values(vc)
+    return (q, k, v), pq, pk, pv, mean
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(mode="topk", budget=0.5),
+    dict(mode="topk", budget=0.25, protected_tokens=200),
+    dict(mode="cdf", budget=0.6, keep_first_column=True, keep_diagonal=True),
+    dict(mode="cdf", budget=0.3),
+    dict(mode="topk", budget=0.1, temporal_radius=1, temporal_spatial_radius=1, video_layout=(4, 250)),
+])
+def test_block_mask_bit_exact(attn, cfg):
+    _, pq, pk, _, _ = _prepared_pair(attn, 1000, 3, seed=21)
+    mc = attn.MaskConfig(**cfg)
+    bm = attn.block_mask(pq, pk, mc)
+    frames, ftok = mc.video_layout or (0, 0)
+    ref = O.block_mask(bits(pq.pooled), pq.similar.cpu().numpy(), bits(pk.pooled), pk.similar.cpu().numpy(),
+                       mode=0 if mc.mode == "topk" else 1, budget=mc.budget,
+                       protected_kb=(mc.protected_tokens + 63) // 64,
+                       flags=int(mc.keep_first_column) | 2 * int(mc.keep_diagonal),
+                       temporal_radius=mc.temporal_radius, temporal_spatial_radius=mc.temporal_spatial_radius,
+                       frames=frames, frame_tokens=ftok, protected_tokens=mc.protected_tokens, q_tokens=pq.tokens)
+    np.testing.assert_array_equal(bm.cpu().numpy().view(np.uint32), ref)
+
+
+def test_block_mask_reference_selector_golden(attn):
+    """Reference fixed-TopK selector (kernels.py:3668-3941) on tie-free inputs."""
+    z = np.load(os.path.join(G, "mask_topk.npz"))
+    q, k = from_bits(z["q"]), from_bits(z["k"])
+    pq = attn.prepare_queries(q)
+    pk, _ = attn.prepare_keys(k, smooth=False)
+    Kb = pk.pooled.shape[1]
+    for topk in (50, 75):
+        for prot in (0, 100):
+            bm = attn.block_mask(pq, pk, attn.MaskConfig("topk", topk / 100.0, protected_tokens=prot))
+            got = O.bitmap_to_bool(bm.cpu().numpy().view(np.uint32), Kb)
+            np.testing.assert_array_equal(got, z[f"topk{topk}_prot{prot}"])
+
+
+def test_bitmap_to_lut_bit_exact(attn):
+    z = np.load(os.path.join(G, "lut.npz"))
+    bm = z["block_map"]
+    H, Qb, Kb = bm.shape
+    words = (Kb + 31) // 32
+    packed = np.zeros((H, Qb, words * 32), np.uint8)
+    packed[..., :Kb] = bm
+    bitmap = np.packbits(packed, axis=-1, bitorder="little").view(np.int32)
+    lut, valid = attn.bitmap_to_lut(torch.from_numpy(bitmap).cuda(), Kb)
+    lo, vo = O.bitmap_to_lut(bitmap.view(np.uint32), Kb)
+    np.testing.assert_array_equal(valid.cpu().numpy(), z["valid"])
+    np.testing.assert_array_equal(lut.cpu().numpy(), lo)
+
+
+def _oracle_attention(pq, pk, pv, bitmap=None):
+    return O.attention(pq.qi8.cpu().numpy(), pq.scale.cpu().numpy(), pq.block, pq.tokens, pk.qi8.cpu().numpy(),
+                       pk.scale.cpu().numpy(), pk.tokens, pv.vt.cpu().numpy(), pv.scale.cpu().numpy(),
+                       None if bitmap is None else bitmap.cpu().numpy().view(np.uint32))
+
+
+def _sdpa(q, k, v):
+    qf, kf, vf = (t.float().permute(1, 0, 2) for t in (q, k, v))
+    s = qf @ kf.transpose(1, 2) / math.sqrt(128)
+    return (s.softmax(-1) @ vf).permute(1, 0, 2)
+
+
+@pytest.mark.parametrize("L,H,Lk", [(1000, 2, None), (128, 1, None), (300, 2, 77), (2048, 1, None), (64, 1, 1)])
+def test_dense_attention_vs_oracle_and_fp32(attn, L, H, Lk):
+    (q, k, v), pq, pk, pv, _ = _prepared_pair(attn, L, H, seed=L + H, Lk=Lk)
+    out = attn.attention(pq, pk, pv)
+    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv))
+    o = out.float().cpu()
+    assert cosine(o, ref) >= 0.999
+    assert rel_l2(o, ref) <= 2e-2
+    exact = _sdpa(q, k, v)
+    assert cosine(o, exact) >= 0.99
+
+
+def test_dense_attention_q_block_64(attn):
+    q, k, v = qkv(700, 2, seed=5)
+    pv = attn.prepare_values(v.cuda())
+    pk, _ = attn.prepare_keys(k.cuda())
+    pq = attn.prepare_queries(q.cuda(), block=64)
+    out = attn.attention(pq, pk, pv).float().cpu()
+    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv))
+    assert cosine(out, ref) >= 0.999 and rel_l2(out, ref) <= 2e-2
+
+
+@pytest.mark.parametrize("cfg", [dict(mode="topk", budget=0.3), dict(mode="cdf", budget=0.6, keep_first_column=True,
+                                                                     keep_diagonal=True)])
+def test_sparse_attention_vs_oracle(attn, cfg):
+    (q, k, v), pq, pk, pv, _ = _prepared_pair(attn, 1500, 2, seed=99)
+    bm = attn.block_mask(pq, pk, attn.MaskConfig(**cfg))
+    out = attn.attention(pq, pk, pv, bm).float().cpu()
+    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv, bm))
+    assert cosine(out, ref) >= 0.999
+    assert rel_l2(out, ref) <= 2e-2
+
+
+def test_backends_are_attention_callables(attn):
+    q, k, v = qkv(513, 2, seed=3)
+    dense = attn.SageAttentionB200()(q.cuda(), k.cuda(), v.cuda())
+    assert dense.shape == (513, 2, 128) and dense.dtype == torch.bfloat16
+    assert cosine(dense.float().cpu(), _sdpa(q, k, v)) >= 0.99
+    sparse = attn.SpargeAttentionB200(attn.MaskConfig("topk", 1.0))(q.cuda(), k.cuda(), v.cuda())
+    assert cosine(sparse.float().cpu(), dense.float().cpu()) >= 0.9999
+
+
+def test_no_device_timeouts_recorded(attn):
+    from h3b import device_status
+    assert device_status(0) == 0

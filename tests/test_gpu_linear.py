@@ -1,0 +1,183 @@
+"""GPU parity of the quantizers, the tcgen05 INT8 GEMM and W4A8 against the CPU oracle.
+
+Bit-exact wherever the computation is integer or has a fixed IEEE order
+(codes, scales, int32 accumulators, bf16 epilogue outputs); bf16 linear outputs
+against the reference's own eager / module outputs within 1e-2 relative L2.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import bits, from_bits, outlier_activations, rel_l2
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from h3b import ops as _ops
+    return _ops
+
+
+def _x(m, k, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return outlier_activations(g, m, k).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m,k", [(1, 256), (77, 512), (300, 4096), (5, 5376), (3, 16384), (2, 32768), (9, 48)])
+def test_quant_rowwise_bit_exact(ops, m, k):
+    x = _x(m, k, seed=m + k)
+    q, s = ops.quantize_int8_rowwise(x.cuda())
+    qo, so = O.quant_rowwise(bits(x))
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), so)
+
+
+def test_quant_rowwise_golden_edge_rows(ops):
+    z = np.load(os.path.join(G, "quant_rowwise.npz"))
+    q, s = ops.quantize_int8_rowwise(from_bits(z["x"]))
+    np.testing.assert_array_equal(q.cpu().numpy(), z["q"])
+    np.testing.assert_allclose(s.cpu().numpy().reshape(-1), z["scale"], rtol=2.5e-7)
+
+
+@pytest.mark.parametrize("act", [None, "gelu_tanh", "swiglu"])
+@pytest.mark.parametrize("m,k", [(1, 256), (130, 4096), (7, 5376), (4, 14336), (3, 16384), (2, 28672)])
+def test_quant_convrot_bit_exact(ops, act, m, k):
+    width = 2 * k if act == "swiglu" else k
+    x = _x(m, width, seed=3 * m + k)
+    q, s = ops.quantize_int8_rowwise_convrot64(x.cuda(), 256, act)
+    qo, so = O.quant_rowwise_convrot(bits(x), {None: 0, "gelu_tanh": 1, "swiglu": 2}[act])
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), so)
+
+
+def test_quant_convrot_strided_rows(ops):
+    x = _x(64, 3 * 1024, seed=11)
+    xs = x.cuda()[:, 1024:2048]
+    q, s = ops.quantize_int8_rowwise_convrot64(xs, 256)
+    qo, so = O.quant_rowwise_convrot(bits(x[:, 1024:2048]), 0)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), so)
+
+
+@pytest.mark.parametrize("convrot", [0, 256])
+@pytest.mark.parametrize("m,k", [(64, 4096), (5, 5376), (3, 16384)])
+def test_rms_adaln_quant_bit_exact(ops, convrot, m, k):
+    g = torch.Generator().manual_seed(m * 7 + k)
+    x = (torch.randn(m, k, generator=g) * 2).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+    sc = (0.2 * torch.randn(3, k, generator=g)).to(torch.bfloat16)
+    sh = (0.2 * torch.randn(3, k, generator=g)).to(torch.bfloat16)
+    segs = ((0, m // 3, 2), (m // 3, m // 2, 0), (m // 2, m, 1)) if m >= 3 else ((0, m, 1),)
+    q, s = ops.rms_adaln_quantize_int8(x.cuda(), w.cuda(), sc.cuda(), sh.cuda(), segs, 1e-5, convrot)
+    seg_row = ops.segment_rows(segs, m, "cpu")
+    qo, so = O.rms_adaln_quant(bits(x), bits(w), bits(sc), bits(sh),
+                               None if seg_row is None else seg_row.numpy(), 1e-5, convrot)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), so)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 16, 16), (100, 72, 256), (300, 520, 4096), (129, 257, 1040), (512, 384, 16384)])
+def test_gemm_i32_bit_exact(ops, m, n, k):
+    g = torch.Generator().manual_seed(m + n + k)
+    a = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int16).to(torch.int8)
+    b = torch.randint(-128, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8)
+    acc = ops.int8_mm_i32(a.cuda(), b.cuda())
+    np.testing.assert_array_equal(acc.cpu().numpy(), O.gemm_i8(a.numpy(), b.numpy()))
+
+
+def test_gemm_i32_full_size_vs_cublas(ops):
+    """BASELINE config 1 shape 4096^3: int32 accumulators equal cuBLASLt's (torch._int_mm)."""
+    g = torch.Generator().manual_seed(0)
+    a = torch.randint(-127, 128, (4096, 4096), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    b = torch.randint(-127, 128, (4096, 4096), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    acc = ops.int8_mm_i32(a, b)
+    ref = torch._int_mm(a, b.t())
+    assert torch.equal(acc, ref)
+
+
+@pytest.mark.parametrize("ws_kind", ["channel", "scalar"])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_linear_epilogue_bit_exact(ops, ws_kind, with_bias):
+    m, n, k = 200, 264, 1024
+    x = _x(m, k, seed=5)
+    g = torch.Generator().manual_seed(9)
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8)
+    ws = (torch.rand(n if ws_kind == "channel" else 1, generator=g) * 1e-3 + 1e-4).float()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16) if with_bias else None
+    out = ops.int8_linear(x.cuda(), w.cuda(), ws.cuda(), None if bias is None else bias.cuda(), convrot=True)
+    ref = O.int8_linear(bits(x), w.numpy(), ws.numpy(), None if bias is None else bias.float().numpy(), convrot=256)
+    np.testing.assert_array_equal(bits(out), ref)
+
+
+def test_gated_residual_bit_exact(ops):
+    m, n, k = 150, 4096, 512
+    x = _x(m, k, seed=6)
+    g = torch.Generator().manual_seed(10)
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8)
+    ws = (torch.rand(n, generator=g) * 1e-3).float()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    gate = (torch.randn(n, generator=g) * 0.5).to(torch.bfloat16)
+    xq, xs = ops.quantize_int8_rowwise_convrot64(x.cuda(), 256)
+    r = res.cuda().clone()
+    ops.int8_linear_gated_residual_(r, gate.cuda(), xq, xs, w.cuda(), ws.cuda(), bias.cuda())
+    qo, so = O.quant_rowwise_convrot(bits(x), 0)
+    ref = O.epilogue(O.gemm_i8(qo, w.numpy()), so, ws.numpy(), bias.float().numpy(), residual=bits(res),
+                     gate=bits(gate))
+    np.testing.assert_array_equal(bits(r), ref)
+
+
+@pytest.mark.parametrize("tag", ["g4_codebook_e4m3", "g16_uniform_f32", "g128_uniform_f32", "g16_codebook_e4m3"])
+def test_w4_decode_matches_reference_golden(ops, tag):
+    z = np.load(os.path.join(G, "w4_decode.npz"))
+    qd = torch.from_numpy(z[tag + "_qdata"]).cuda()
+    sr = z[tag + "_srel"]
+    srt = (torch.from_numpy(sr).view(torch.float8_e4m3fn) if sr.dtype == np.uint8 else torch.from_numpy(sr)).cuda()
+    cb = z[tag + "_codebook"]
+    out = ops.dequant_int4_grouped_to_int8(qd, srt, torch.from_numpy(cb).cuda() if cb.size else None,
+                                           int(z[tag + "_G"]))
+    np.testing.assert_array_equal(out.cpu().numpy(), z[tag + "_out"])
+
+
+def test_linear_vs_reference_outputs(ops):
+    """Reference eager int8_linear / ConvRotInt8Linear / W4A8 outputs (golden) within 1e-2 rel-L2."""
+    z = np.load(os.path.join(G, "linear.npz"))
+    x = from_bits(z["x"])
+    wq = torch.from_numpy(z["wq"]).cuda()
+    ws = torch.from_numpy(z["ws"]).cuda()
+    bias = from_bits(z["bias"])
+    out = ops.int8_linear(x, wq, ws, bias, convrot=False)
+    assert rel_l2(out.float(), from_bits(z["out_eager"]).float()) < 1e-2
+    out_r = ops.int8_linear(x, wq, ws, bias, convrot=True)
+    assert rel_l2(out_r.float(), from_bits(z["out_eager_rot"]).float()) < 1e-2
+    assert rel_l2(out_r.float(), from_bits(z["out_module_rot"]).float()) < 2e-2
+    w4 = ops.w4a8_int8_linear(x, torch.from_numpy(z["w4_qdata"]).cuda(), torch.from_numpy(z["w4_srel"]).cuda(),
+                              torch.from_numpy(z["w4_sch"]).cuda(), None, None, bias, int(z["w4_G"]), 256)
+    assert rel_l2(w4.float(), from_bits(z["out_w4_eager"]).float()) < 1e-2
+    assert rel_l2(w4.float(), from_bits(z["out_w4_module"]).float()) < 2e-2
+
+
+def test_module_injection_matches_reference_module(ops):
+    """h3b_int8_kernel injected into the engine's Int8Kernel slot reproduces the
+    oracle bit for bit (same quant + GEMM + epilogue)."""
+    from h3b import h3b_int8_kernel
+    z = np.load(os.path.join(G, "linear.npz"))
+    x = from_bits(z["x"])
+    out = h3b_int8_kernel(x, torch.from_numpy(z["wq"]).cuda(), torch.from_numpy(z["ws"]).cuda(),
+                          from_bits(z["bias"]), 256)
+    ref = O.int8_linear(z["x"], z["wq"], z["ws"], O.bf16_bits_to_f32(z["bias"]), convrot=256)
+    np.testing.assert_array_equal(bits(out), ref)
+
+
+def test_no_device_timeouts_recorded(ops):
+    from h3b import device_status
+    assert device_status(0) == 0

@@ -1,0 +1,262 @@
+// attn_prep.cu -- quantized-attention preparation kernels.
+//
+//  key mean     per-(head, channel) mean of K over the sequence (K smoothing),
+//               double accumulation in a fixed order (1024-token chunks, then
+//               the chunk sums), replacing hnd_compatible_key_mean_nhd
+//               (model/sparge_nhd.py:26-48)
+//  pool/sim/quant  Sparge per-block pooled mean, self-similarity flag and
+//               per-block INT8 quantization (model/sparge_nhd.py:51-160), on
+//               NHD input with any row stride (reads Q/K straight out of the
+//               fused QKV projection output)
+//  value fp8    per-(head, channel) absmax, V * 2.25/absmax -> E4M3, transposed
+//               to [H, 128, Lpad] (model/compact_fp8.py:13-300)
+// Every reduction runs in the order the CPU oracle restates, so results are
+// bit-identical to it.
+#include "h3b_kernels.cuh"
+
+namespace h3b {
+
+constexpr int kKeyMeanChunk = 1024;
+constexpr int kD = 128;
+
+// ------------------------------------------------------------------ key mean
+
+__global__ void __launch_bounds__(256) key_mean_partial_kernel(const uint16_t* __restrict__ k, int64_t L, int cols,
+                                                                int64_t stride, double* __restrict__ part) {
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const int64_t r0 = (int64_t)blockIdx.x * kKeyMeanChunk;
+  const int64_t r1 = r0 + kKeyMeanChunk < L ? r0 + kKeyMeanChunk : L;
+  double s = 0.0;
+  const uint16_t* p = k + r0 * stride + c;
+  int64_t r = r0;
+  for (; r + 4 <= r1; r += 4) {
+    const float a0 = bf16_bits_to_f32(p[0]), a1 = bf16_bits_to_f32(p[stride]);
+    const float a2 = bf16_bits_to_f32(p[2 * stride]), a3 = bf16_bits_to_f32(p[3 * stride]);
+    s = __dadd_rn(s, (double)a0);
+    s = __dadd_rn(s, (double)a1);
+    s = __dadd_rn(s, (double)a2);
+    s = __dadd_rn(s, (double)a3);
+    p += 4 * stride;
+  }
+  for (; r < r1; ++r, p += stride) s = __dadd_rn(s, (double)bf16_bits_to_f32(p[0]));
+  part[(int64_t)blockIdx.x * cols + c] = s;
+}
+
+__global__ void __launch_bounds__(256) key_mean_final_kernel(const double* __restrict__ part, int chunks, int cols,
+                                                              int64_t L, uint16_t* __restrict__ mean) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  double s = 0.0;
+  for (int i = 0; i < chunks; ++i) s = __dadd_rn(s, part[(int64_t)i * cols + c]);
+  mean[c] = f32_to_bf16_bits(__double2float_rn(__ddiv_rn(s, (double)L)));
+}
+
+int64_t key_mean_workspace(int64_t L, int64_t H) {
+  return ((L + kKeyMeanChunk - 1) / kKeyMeanChunk) * H * kD * (int64_t)sizeof(double);
+}
+
+cudaError_t launch_key_mean(const void* k, int64_t L, int64_t H, int64_t stride, void* mean, void* ws,
+                            cudaStream_t s) {
+  const int cols = (int)(H * kD);
+  const int chunks = (int)((L + kKeyMeanChunk - 1) / kKeyMeanChunk);
+  dim3 g1(chunks, (cols + 255) / 256);
+  key_mean_partial_kernel<<<g1, 256, 0, s>>>(static_cast<const uint16_t*>(k), L, cols, stride,
+                                             static_cast<double*>(ws));
+  key_mean_final_kernel<<<(cols + 255) / 256, 256, 0, s>>>(static_cast<const double*>(ws), chunks, cols, L,
+                                                             static_cast<uint16_t*>(mean));
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ pool / sim / quant
+
+
+__device__ __forceinline__ void load4_row(const PoolArgs& a, int64_t row, int h, int lane, const float (&mean4)[4],
+                                          float (&v)[4]) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(a.x + row * a.stride + (int64_t)h * kD + 4 * lane);
+  v[0] = __uint_as_float(raw.x << 16);
+  v[1] = __uint_as_float(raw.x & 0xffff0000u);
+  v[2] = __uint_as_float(raw.y << 16);
+  v[3] = __uint_as_float(raw.y & 0xffff0000u);
+  if (a.mean) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bf16r(__fsub_rn(v[i], mean4[i]));
+  }
+}
+
+// One CTA of four warps per (block, head); lane l owns channels 4l..4l+3 and
+// warp w walks rows w, w+4, ... of the block.
+__global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
+  __shared__ float pp_s[4][kD], sp_s[4][kD];
+  __shared__ float amax_s[4];
+  __shared__ float scale_s;
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = (int64_t)b * a.blk;
+  const int valid = (int)((a.L - r0) < a.blk ? (a.L - r0) : a.blk);
+  const int nb = (int)((a.L + a.blk - 1) / a.blk);
+
+  float mean4[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.mean) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(a.mean + h * kD + 4 * lane);
+    mean4[0] = __uint_as_float(raw.x << 16);
+    mean4[1] = __uint_as_float(raw.x & 0xffff0000u);
+    mean4[2] = __uint_as_float(raw.y << 16);
+    mean4[3] = __uint_as_float(raw.y & 0xffff0000u);
+  }
+
+  float pp[4] = {0.f, 0.f, 0.f, 0.f}, sp[4] = {0.f, 0.f, 0.f, 0.f}, amax = 0.f;
+  for (int r = warp; r < valid; r += 4) {
+    float v[4];
+    load4_row(a, r0 + r, h, lane, mean4, v);
+    float sq = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])), __fmul_rn(v[2], v[2])),
+                         __fmul_rn(v[3], v[3]));
+    const float norm = __fsqrt_rn(warp_butterfly_sum(sq));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      pp[i] = __fadd_rn(pp[i], v[i]);
+      sp[i] = __fadd_rn(sp[i], f16r(__fdiv_rn(v[i], norm)));
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    pp_s[warp][4 * lane + i] = pp[i];
+    sp_s[warp][4 * lane + i] = sp[i];
+  }
+  if (lane == 0) amax_s[warp] = amax;
+  __syncthreads();
+  if (warp == 0) {
+    float s2[4];
+    uint16_t pooled[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int d = 4 * lane + i;
+      const float ps = __fadd_rn(__fadd_rn(pp_s[0][d], pp_s[2][d]), __fadd_rn(pp_s[1][d], pp_s[3][d]));
+      const float ss = __fadd_rn(__fadd_rn(sp_s[0][d], sp_s[2][d]), __fadd_rn(sp_s[1][d], sp_s[3][d]));
+      pooled[i] = f32_to_bf16_bits(__fdiv_rn(ps, (float)valid));
+      s2[i] = __fmul_rn(ss, ss);
+    }
+    *reinterpret_cast<uint2*>(a.pooled + ((int64_t)h * nb + b) * kD + 4 * lane) =
+        make_uint2((uint32_t)pooled[0] | ((uint32_t)pooled[1] << 16), (uint32_t)pooled[2] | ((uint32_t)pooled[3] << 16));
+    const float g = warp_butterfly_sum(__fadd_rn(__fadd_rn(__fadd_rn(s2[0], s2[1]), s2[2]), s2[3]));
+    const float simv = __fdiv_rn(g, (float)(valid * valid));
+    const float am = fmaxf(fmaxf(amax_s[0], amax_s[1]), fmaxf(amax_s[2], amax_s[3]));
+    const float sc = __fadd_rn(__fdiv_rn(am, 127.0f), 1e-7f);
+    if (lane == 0) {
+      a.similar[(int64_t)h * nb + b] = (uint8_t)(valid == a.blk && simv > a.thr[h]);
+      a.scale[(int64_t)h * nb + b] = sc;
+      scale_s = sc;
+    }
+  }
+  __syncthreads();
+  const float sc = scale_s;
+  for (int r = warp; r < a.blk; r += 4) {
+    uint32_t word = 0;
+    if (r < valid) {
+      float v[4];
+      load4_row(a, r0 + r, h, lane, mean4, v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float t = __fdiv_rn(v[i], sc);
+        t = __fadd_rn(t, t >= 0.0f ? 0.5f : -0.5f);
+        float tr = fminf(127.0f, fmaxf(-127.0f, truncf(t)));
+        word |= ((uint32_t)(int)tr & 0xffu) << (8 * i);
+      }
+    }
+    *reinterpret_cast<uint32_t*>(a.q + ((int64_t)h * a.Lpad + r0 + r) * kD + 4 * lane) = word;
+  }
+}
+
+cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s) {
+  const int nb = (int)((a.L + a.blk - 1) / a.blk);
+  dim3 grid(nb, a.H);
+  pool_sim_quant_kernel<<<grid, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ value fp8
+
+constexpr int kAbsRows = 512;
+
+__global__ void __launch_bounds__(256) value_absmax_kernel(const uint16_t* __restrict__ v, int64_t L, int cols,
+                                                            int64_t stride, unsigned int* __restrict__ amax_bits) {
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const int64_t r0 = (int64_t)blockIdx.x * kAbsRows;
+  const int64_t r1 = r0 + kAbsRows < L ? r0 + kAbsRows : L;
+  float m = 0.f;
+  const uint16_t* p = v + r0 * stride + c;
+  for (int64_t r = r0; r < r1; ++r, p += stride) m = fmaxf(m, fabsf(bf16_bits_to_f32(*p)));
+  atomicMax(amax_bits + c, __float_as_uint(m));  // non-negative floats order like their bits
+}
+
+// One CTA per (128-token tile, head): read V[128 tokens][128 ch] (bf16) into
+// shared memory, write vt[h][ch][tile] as E4M3, 128 bytes per channel row.
+__global__ void __launch_bounds__(256) value_fp8_kernel(const uint16_t* __restrict__ v, int64_t L, int H,
+                                                         int64_t stride, int64_t Lpad,
+                                                         const float* __restrict__ amax, uint8_t* __restrict__ vt) {
+  __shared__ uint16_t tile[128][kD + 2];
+  __shared__ float mul_s[kD];
+  const int h = blockIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.x * 128;
+  for (int i = threadIdx.x; i < 128 * (kD / 8); i += blockDim.x) {
+    const int r = i / (kD / 8), c8 = (i % (kD / 8)) * 8;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (t0 + r < L) raw = *reinterpret_cast<const uint4*>(v + (t0 + r) * stride + (int64_t)h * kD + c8);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tile[r][c8 + 2 * j] = (uint16_t)(w[j] & 0xffffu);
+      tile[r][c8 + 2 * j + 1] = (uint16_t)(w[j] >> 16);
+    }
+  }
+  if (threadIdx.x < kD) {
+    const float am = amax[h * kD + threadIdx.x];
+    mul_s[threadIdx.x] = am > 0.f ? __fdiv_rn(2.25f, am) : 0.f;
+  }
+  __syncthreads();
+  // thread -> (channel, half of the 128 tokens): 64 bytes out
+  const int d = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const float mul = mul_s[d];
+  uint32_t out[16];
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const int r = half * 64 + 4 * w + j;
+      const float a0 = (t0 + r < L) ? __fmul_rn(bf16_bits_to_f32(tile[r][d]), mul) : 0.f;
+      const float a1 = (t0 + r + 1 < L) ? __fmul_rn(bf16_bits_to_f32(tile[r + 1][d]), mul) : 0.f;
+      word |= (uint32_t)f32x2_to_e4m3x2(a0, a1) << (8 * j);
+    }
+    out[w] = word;
+  }
+  uint8_t* dst = vt + ((int64_t)h * kD + d) * Lpad + t0 + half * 64;
+#pragma unroll
+  for (int w = 0; w < 16; w += 4) *reinterpret_cast<uint4*>(dst + 4 * w) = make_uint4(out[w], out[w + 1], out[w + 2], out[w + 3]);
+}
+
+__global__ void value_scale_final_kernel(float* vscale, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) vscale[i] = __fdiv_rn(vscale[i], 2.25f);
+}
+
+cudaError_t launch_value_fp8(const void* v, int64_t L, int64_t H, int64_t stride, int64_t Lpad, void* vt,
+                             void* vscale, cudaStream_t s) {
+  const int cols = (int)(H * kD);
+  cudaError_t e = cudaMemsetAsync(vscale, 0, sizeof(float) * cols, s);
+  if (e != cudaSuccess) return e;
+  dim3 g1((unsigned)((L + kAbsRows - 1) / kAbsRows), (cols + 255) / 256);
+  value_absmax_kernel<<<g1, 256, 0, s>>>(static_cast<const uint16_t*>(v), L, cols, stride,
+                                         static_cast<unsigned int*>(vscale));
+  dim3 g2((unsigned)(Lpad / 128), (unsigned)H);
+  value_fp8_kernel<<<g2, 256, 0, s>>>(static_cast<const uint16_t*>(v), L, (int)H, stride, Lpad,
+                                      static_cast<const float*>(vscale), static_cast<uint8_t*>(vt));
+  value_scale_final_kernel<<<(cols + 255) / 256, 256, 0, s>>>(static_cast<float*>(vscale), cols);
+  return cudaGetLastError();
+}
+
+}  // namespace h3b

@@ -1,0 +1,321 @@
+// gemm_i8.cu -- INT8 x INT8 -> INT32 GEMM on the sm_100 tensor cores
+// (tcgen05.mma kind::i8, accumulators in tensor memory), with the linear's
+// dequant epilogue fused:  D = bf16(float(acc) * xs[m] * ws[n] + bias[n]),
+// optionally added into a bf16 residual stream with a per-column gate.
+//
+// Persistent, warp-specialized CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A [128 x 128 B] and B [BN x 128 B] tiles into a
+//               kStages-deep shared-memory ring (128-byte swizzle, no multicast)
+//   warp 1      TMEM allocator + MMA issuer (one thread): 4 x K=32 MMAs per
+//               stage into one of two TMEM accumulators (2 x BN columns)
+//   warps 2..5  epilogue: tcgen05.ld of 32 columns at a time, dequant, store;
+//               the other accumulator is being filled meanwhile
+// Tiles are walked M-major (all N tiles of one 128-row band before the next
+// band) so the A band and the whole weight matrix stay L2-resident.
+#include "h3b_kernels.cuh"
+
+namespace h3b {
+
+constexpr int kBM = 128;
+constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle row
+constexpr int kGemmThreads = 192;
+
+
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kTotal = kBarOffset + 256 + 1024;  // barriers + alignment slack
+};
+
+__device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, int n0, const GemmArgs& a,
+                                                float xs_m, int kind) {
+  const int N = a.N;
+  if (kind == kEpiInt32) {
+    int32_t* dst = a.out_i32 + (int64_t)m * a.out_stride + n0;
+    if (n0 + 32 <= N && (a.out_stride % 4) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+    } else {
+      for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = (int)r[j];
+    }
+    return;
+  }
+  float y[32];
+  const bool full = n0 + 32 <= N;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int n = n0 + j;
+    const int nn = n < N ? n : N - 1;
+    const float w = a.ws_scalar ? a.ws[0] : __ldg(a.ws + nn);
+    const float v = __fmul_rn((float)(int)r[j], xs_m);
+    y[j] = a.bias ? fmaf(v, w, __ldg(a.bias + nn)) : __fmul_rn(v, w);
+  }
+  uint16_t* dst = a.out + (int64_t)m * a.out_stride + n0;
+  const bool vec = full && ((a.out_stride & 7) == 0) && ((n0 & 7) == 0);
+  if (kind == kEpiStore) {
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 p;
+        p.x = (uint32_t)f32_to_bf16_bits(y[j]) | ((uint32_t)f32_to_bf16_bits(y[j + 1]) << 16);
+        p.y = (uint32_t)f32_to_bf16_bits(y[j + 2]) | ((uint32_t)f32_to_bf16_bits(y[j + 3]) << 16);
+        p.z = (uint32_t)f32_to_bf16_bits(y[j + 4]) | ((uint32_t)f32_to_bf16_bits(y[j + 5]) << 16);
+        p.w = (uint32_t)f32_to_bf16_bits(y[j + 6]) | ((uint32_t)f32_to_bf16_bits(y[j + 7]) << 16);
+        *reinterpret_cast<uint4*>(dst + j) = p;
+      }
+    } else {
+      for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = f32_to_bf16_bits(y[j]);
+    }
+  } else {  // gated residual, in place
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 rv = *reinterpret_cast<const uint4*>(dst + j);
+        uint4 gv = __ldg(reinterpret_cast<const uint4*>(a.gate + n0 + j));
+        uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w}, ow[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float r0 = __uint_as_float(rw[h] << 16), r1 = __uint_as_float(rw[h] & 0xffff0000u);
+          float g0 = __uint_as_float(gw[h] << 16), g1 = __uint_as_float(gw[h] & 0xffff0000u);
+          float o0 = __fadd_rn(r0, __fmul_rn(bf16r(y[j + 2 * h]), g0));
+          float o1 = __fadd_rn(r1, __fmul_rn(bf16r(y[j + 2 * h + 1]), g1));
+          ow[h] = (uint32_t)f32_to_bf16_bits(o0) | ((uint32_t)f32_to_bf16_bits(o1) << 16);
+        }
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
+    } else {
+      for (int j = 0; j < 32 && n0 + j < N; ++j) {
+        float rr = bf16_bits_to_f32(dst[j]);
+        float g = bf16_bits_to_f32(a.gate[n0 + j]);
+        dst[j] = f32_to_bf16_bits(__fadd_rn(rr, __fmul_rn(bf16r(y[j]), g)));
+      }
+    }
+  }
+}
+
+template <int BN, int KIND>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs a) {
+  using S = GemmSmem<BN>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;   // [2]
+  uint64_t* tempty = tfull + 2;        // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (a.M + kBM - 1) / kBM, num_n = (a.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int num_k = (a.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int mb = t / num_n, nb = t % num_n;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          tma_load_2d(sa, &tmA, &full[stage], kb * kBK, mb * kBM);
+          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nb * BN);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: every filled stage must have been consumed (its TMA landed and
+      // its MMAs finished) before the CTA may exit.  Bounded like every wait.
+      for (int s = 0; s < kStages; ++s) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+          const uint64_t da = sdesc_kmajor_sw128(sa), db = sdesc_kmajor_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k) {
+            // +32 bytes of K per MMA: +2 in the descriptor's 16-byte address units
+            mma_i8_ss(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int mb = t / num_n, nb = t % num_n;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+      tc_fence_after();
+      const int m = mb * kBM + row_in_tile;
+      const float xs_m = (KIND != kEpiInt32 && m < a.M) ? __ldg(a.xs + m) : 0.0f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)(c * 32), r);
+        tmem_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        const int n0 = nb * BN + c * 32;
+        if (m < a.M && n0 < a.N) epi_store_chunk(r, m, n0, a, xs_m, KIND);
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D byte tensor [rows, cols] with row stride `stride` bytes; box [box_rows, box_cols]
+// with 128-byte swizzle (box_cols * elem must be <= 128).
+bool make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
+                  uint64_t rows, uint64_t stride_bytes, uint32_t box_cols, uint32_t box_rows,
+                  CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = get_encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int KIND>
+static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t s) {
+  using S = GemmSmem<BN>;
+  auto k = gemm_i8_kernel<BN, KIND>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+  if (e != cudaSuccess) return e;
+  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  k<<<grid, kGemmThreads, S::kTotal, s>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+// Returns 0 on success, 1 if a tensor map could not be encoded, else a CUDA error.
+int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t s, cudaError_t* err) {
+  const int tiles256 = ((a.M + kBM - 1) / kBM) * ((a.N + 255) / 256);
+  const int BN = (tiles256 >= num_sms() || a.N > 128) ? 256 : 128;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K, kBK, kBM,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return 1;
+  if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, kBK,
+                    (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return 1;
+  cudaError_t e;
+  if (BN == 256) {
+    e = kind == kEpiStore      ? launch_gemm_bn<256, kEpiStore>(ta, tb, a, s)
+        : kind == kEpiResidual ? launch_gemm_bn<256, kEpiResidual>(ta, tb, a, s)
+                               : launch_gemm_bn<256, kEpiInt32>(ta, tb, a, s);
+  } else {
+    e = kind == kEpiStore      ? launch_gemm_bn<128, kEpiStore>(ta, tb, a, s)
+        : kind == kEpiResidual ? launch_gemm_bn<128, kEpiResidual>(ta, tb, a, s)
+                               : launch_gemm_bn<128, kEpiInt32>(ta, tb, a, s);
+  }
+  *err = e;
+  return e == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace h3b

@@ -1,0 +1,95 @@
+// h3b_kernels.cuh -- argument structs and host launchers shared between the
+// kernel translation units and the C ABI (capi.cu).
+#pragma once
+
+#include "h3b_common.cuh"
+
+namespace h3b {
+
+struct QuantArgs {
+  const uint16_t* x;          // bf16 [rows, x_stride]
+  int64_t x_stride;           // elements between rows of x
+  int K;                      // quantized width
+  int act;                    // 0 none, 1 gelu_tanh, 2 swiglu ([gate | up], 2K wide)
+  int8_t* q;                  // [rows, K]
+  float* scales;              // [rows]
+  const uint16_t* norm_w;     // fused RMSNorm + AdaLN: bf16 [K]
+  const uint16_t* scale_tab;  // bf16 [R, K]
+  const uint16_t* shift_tab;  // bf16 [R, K]
+  const int32_t* seg_row;     // [rows] or null (table row 0)
+  float eps;
+};
+cudaError_t launch_quant(const QuantArgs& a, int64_t rows, int mode, bool rms, cudaStream_t s);
+int quant_threads_for(int K);
+
+enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiInt32 = 2 };
+struct GemmArgs {
+  int M, N, K;
+  const float* xs;
+  const float* ws;
+  int ws_scalar;
+  const float* bias;
+  uint16_t* out;      // bf16 output or residual (in place)
+  int32_t* out_i32;   // raw accumulators
+  int64_t out_stride;
+  const uint16_t* gate;
+};
+// 0 ok, 1 tensor-map encoding failed, 2 CUDA launch error (*err)
+int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t s, cudaError_t* err);
+bool make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
+                  uint64_t rows, uint64_t stride_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw);
+
+cudaError_t launch_w4_decode(const void* qw, const void* s_rel, int s_rel_kind, const void* codebook, void* out,
+                             int64_t N, int64_t K, int64_t G, cudaStream_t s);
+
+int64_t key_mean_workspace(int64_t L, int64_t H);
+cudaError_t launch_key_mean(const void* k, int64_t L, int64_t H, int64_t stride, void* mean, void* ws, cudaStream_t s);
+
+struct PoolArgs {
+  const uint16_t* x;
+  int64_t L, stride, Lpad;
+  int H, blk;
+  const uint16_t* mean;  // bf16 [H, 128] or null
+  const float* thr;
+  uint16_t* pooled;      // [H, nb, 128]
+  uint8_t* similar;      // [H, nb]
+  int8_t* q;             // [H, Lpad, 128]
+  float* scale;          // [H, nb]
+};
+cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s);
+cudaError_t launch_value_fp8(const void* v, int64_t L, int64_t H, int64_t stride, int64_t Lpad, void* vt,
+                             void* vscale, cudaStream_t s);
+
+struct MaskArgs {
+  const uint16_t* pq;   // [H, Qb, 128]
+  const uint8_t* simq;  // [H, Qb]
+  const uint16_t* pk;   // [H, Kb, 128]
+  const uint8_t* simk;  // [H, Kb]
+  int64_t Qb, Kb;
+  int mode;
+  const float* budget;  // device [H]
+  int64_t protected_kb;
+  int first_col, diag;
+  int temporal_radius, temporal_spatial_radius;
+  int64_t frames, frame_tokens, protected_tokens, query_tokens;
+  uint32_t* bitmap;
+};
+cudaError_t launch_block_mask(const MaskArgs& a, int64_t H, cudaStream_t s);
+cudaError_t launch_bitmap_to_lut(const void* bm, int64_t rows, int64_t Kb, void* lut, void* valid, cudaStream_t s);
+
+struct AttnArgs {
+  int H;
+  int64_t Lq, Lqpad, Lk, Lkpad;
+  int Kb, words, q_block, nqs;
+  const float* q_scale;
+  const float* k_scale;
+  const float* v_scale;
+  const uint32_t* bitmap;
+  float scale_log2;  // sm_scale * log2(e)
+  uint16_t* out;
+  int64_t out_stride;
+};
+int launch_attention(const void* q, const void* k, const void* vt, const AttnArgs& a, cudaStream_t s,
+                     cudaError_t* err);
+
+}  // namespace h3b
