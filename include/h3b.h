@@ -151,6 +151,19 @@ int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride
                        int block, const void* thr, void* pooled, void* similar, void* qi8, void* scale,
                        int64_t Lpad, void* stream);
 
+/* Per-head RMSNorm (weight, eps) of Q and K followed by split-half partial
+ * RoPE over the first rot_dim channels, in place on bf16 projection rows:
+ * qkv [L, row_stride], Q heads at column q_offset, K heads at k_offset (128
+ * channels per head); q_weight / k_weight bf16 [128]; cos_table / sin_table
+ * bf16 [L, rot_dim/2] (the packed split-half rotation of the token).
+ * n = bf16(x * inv_rms * w); out_d = bf16(n_d cos - n_{d+r} sin),
+ * out_{d+r} = bf16(n_d sin + n_{d+r} cos), r = rot_dim/2.
+ * Replaces apply_qknorm_rope / rms_rope_split_half_ (model/layers.py:72-149,
+ * comfy_kitchen backends/cuda/ops/rms_rope.cu:38-384). */
+int h3b_qk_rmsnorm_rope(void* qkv, int64_t L, int64_t H, int64_t row_stride, int64_t q_offset, int64_t k_offset,
+                        const void* q_weight, const void* k_weight, const void* cos_table, const void* sin_table,
+                        int rot_dim, float eps, void* stream);
+
 /* V -> FP8 E4M3 per-(head, channel) scaled by 2.25/absmax, transposed to
  * vt [H, 128, Lpad] (token index innermost, rows >= L zero); vscale: f32
  * [H, 128] = absmax/2.25.  v: bf16 NHD [L, H*128], row stride v_row_stride.
@@ -166,7 +179,7 @@ typedef struct h3b_mask_params {
   int mode;                     /* 0 fixed Top-K: count = (int64)(budget[h]*Kb)
                                    1 top-CDF: smallest-rank prefix with cumulative
                                      probability <= budget[h] */
-  const float* budget;          /* host or device? -> device f32 [H] */
+  const float* budget;          /* device memory, f32 [H]: Top-K fraction or CDF threshold */
   int64_t protected_key_blocks; /* first blocks always kept (protected prefix) */
   int keep_first_column;        /* always keep K block 0 */
   int keep_diagonal;            /* always keep K blocks 2i, 2i+1 for Q block i */

@@ -516,6 +516,41 @@ void h3bo_pool_sim_quant(const uint16_t* x, int64_t L, int64_t H, const uint16_t
     free(v);
 }
 
+/* Per-head RMSNorm + split-half partial RoPE, in place (model/layers.py:72-149):
+ * n = bf16((x * inv) * w), inv = 1/sqrt(sum(x^2)/128 + eps) with the sum in the
+ * warp order of warp_sum128; then for d < r = rot/2:
+ * out_d = bf16(n_d c - n_{d+r} s), out_{d+r} = bf16(n_d s + n_{d+r} c); channels
+ * >= rot pass through normalised; c, s from the bf16 tables [L, rot/2]. */
+static void rms_rope_vec(uint16_t* p, const uint16_t* w, const uint16_t* ct, const uint16_t* st, int rot, float eps) {
+    float v[128], sq[128], n[128];
+    for (int d = 0; d < 128; ++d) { v[d] = bf16_to_f32(p[d]); sq[d] = v[d] * v[d]; }
+    float ss = warp_sum128(sq);
+    float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+    for (int d = 0; d < 128; ++d) n[d] = bf16r(v[d] * inv * bf16_to_f32(w[d]));
+    int half = rot / 2;
+    for (int d = 0; d < 128; ++d) {
+        float o = n[d];
+        if (d < half) {
+            float c = bf16_to_f32(ct[d]), s = bf16_to_f32(st[d]);
+            o = bf16r(n[d] * c - n[d + half] * s);
+        } else if (d < rot) {
+            float c = bf16_to_f32(ct[d - half]), s = bf16_to_f32(st[d - half]);
+            o = bf16r(n[d - half] * s + n[d] * c);
+        }
+        p[d] = f32_to_bf16(o);
+    }
+}
+void h3bo_qk_rmsnorm_rope(uint16_t* x, int64_t L, int64_t H, int64_t stride, int64_t q_off, int64_t k_off,
+                          const uint16_t* qw, const uint16_t* kw, const uint16_t* ct, const uint16_t* st,
+                          int rot, float eps) {
+    int half = rot / 2;
+    for (int64_t t = 0; t < L; ++t)
+        for (int64_t h = 0; h < H; ++h) {
+            rms_rope_vec(x + t * stride + q_off + h * 128, qw, ct + t * half, st + t * half, rot, eps);
+            rms_rope_vec(x + t * stride + k_off + h * 128, kw, ct + t * half, st + t * half, rot, eps);
+        }
+}
+
 /* V -> FP8 E4M3 with per-(head, channel) scale absmax/2.25, transposed to
  * [H, 128, Lpad] (compact_fp8.py:205-300, without the sm89 16-row permutation).
  * scaled = float(v) * (2.25 / absmax); an all-zero channel writes zeros, scale 0. */

@@ -206,6 +206,15 @@ def pool_sim_quant(x_bf16, block: int, thr, mean=None):
     return pooled, sim, q, sc
 
 
+def qk_rmsnorm_rope(qkv_bf16, H, q_off, k_off, qw, kw, cos_t, sin_t, rot=128, eps=1e-6):
+    x = np.array(qkv_bf16, dtype=np.uint16, copy=True)
+    L, stride = x.shape
+    lib().h3bo_qk_rmsnorm_rope(_p(x), I64(L), I64(H), I64(stride), I64(q_off), I64(k_off),
+                               _p(_c(qw, np.uint16)), _p(_c(kw, np.uint16)), _p(_c(cos_t, np.uint16)),
+                               _p(_c(sin_t, np.uint16)), ctypes.c_int(rot), ctypes.c_float(eps))
+    return x
+
+
 def value_fp8(v_bf16, Lpad=None):
     v = _c(v_bf16, np.uint16)
     L, H, D = v.shape

@@ -42,6 +42,21 @@ def qkv(L, H, seed, k_offset=True, Lk=None):
     return q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
 
 
+@pytest.mark.parametrize("rot", [128, 64, 96])
+def test_qk_rmsnorm_rope_bit_exact(attn, rot):
+    from h3b import ops
+    g = torch.Generator().manual_seed(rot)
+    L, H = 300, 3
+    qkv = (torch.randn(L, 3 * H * 128 + 8, generator=g) * 2).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    ang = torch.rand(L, rot // 2, generator=g) * 6
+    ct, st = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    got = ops.qk_rmsnorm_rope_(qkv.cuda(), H, 0, H * 128, qw.cuda(), kw.cuda(), ct.cuda(), st.cuda(), 1e-6)
+    ref = O.qk_rmsnorm_rope(bits(qkv), H, 0, H * 128, bits(qw), bits(kw), bits(ct), bits(st), rot, 1e-6)
+    np.testing.assert_array_equal(bits(got), ref)
+
+
 @pytest.mark.parametrize("L,H", [(197, 4), (1000, 2), (4096, 1)])
 def test_key_mean_bit_exact(attn, L, H):
     _, k, _ = qkv(L, H, seed=L)

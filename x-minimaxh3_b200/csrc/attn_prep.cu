@@ -177,6 +177,64 @@ cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ q/k RMSNorm + RoPE
+
+// One warp per (token, q|k, head), in place on the projection output rows:
+// n = bf16((x * inv_rms) * w);  for d < rot/2 with its partner e = d + rot/2:
+//   out_d = bf16(n_d cos - n_e sin), out_e = bf16(n_d sin + n_e cos)
+// (model/layers.py:72-149 split-half partial RoPE after per-head RMSNorm).
+__global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(QkRopeArgs a) {
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t per_tok = 2 * (int64_t)a.H;
+  if (wid >= a.L * per_tok) return;
+  const int64_t t = wid / per_tok;
+  const int rem = (int)(wid % per_tok);
+  const bool is_k = rem >= a.H;
+  const int h = is_k ? rem - a.H : rem;
+  uint16_t* p = a.x + t * a.stride + (is_k ? a.k_off : a.q_off) + (int64_t)h * kD + 4 * lane;
+  const uint16_t* w = (is_k ? a.kw : a.qw) + 4 * lane;
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const uint2 wr = *reinterpret_cast<const uint2*>(w);
+  float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u), __uint_as_float(raw.y << 16),
+                __uint_as_float(raw.y & 0xffff0000u)};
+  const float wv[4] = {__uint_as_float(wr.x << 16), __uint_as_float(wr.x & 0xffff0000u),
+                       __uint_as_float(wr.y << 16), __uint_as_float(wr.y & 0xffff0000u)};
+  const float sq = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])), __fmul_rn(v[2], v[2])),
+                             __fmul_rn(v[3], v[3]));
+  const float ss = warp_butterfly_sum(sq);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = bf16r(__fmul_rn(__fmul_rn(v[i], inv), wv[i]));
+  const int half = a.rot_dim >> 1, d0 = 4 * lane;
+  const bool first = d0 < half, rot = d0 < a.rot_dim;
+  const int src = first ? lane + (half >> 2) : lane - (half >> 2);
+  float o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float partner = __shfl_sync(0xffffffffu, n[i], rot ? src : lane);
+    if (rot) {
+      const int j = (first ? d0 : d0 - half) + i;
+      const float c = bf16_bits_to_f32(a.cos_t[t * half + j]);
+      const float s = bf16_bits_to_f32(a.sin_t[t * half + j]);
+      o[i] = first ? bf16r(__fsub_rn(__fmul_rn(n[i], c), __fmul_rn(partner, s)))
+                   : bf16r(__fadd_rn(__fmul_rn(partner, s), __fmul_rn(n[i], c)));
+    } else {
+      o[i] = n[i];
+    }
+  }
+  *reinterpret_cast<uint2*>(p) =
+      make_uint2((uint32_t)f32_to_bf16_bits(o[0]) | ((uint32_t)f32_to_bf16_bits(o[1]) << 16),
+                 (uint32_t)f32_to_bf16_bits(o[2]) | ((uint32_t)f32_to_bf16_bits(o[3]) << 16));
+}
+
+cudaError_t launch_qk_rmsnorm_rope(const QkRopeArgs& a, cudaStream_t s) {
+  const int64_t warps = a.L * 2 * a.H;
+  qk_rmsnorm_rope_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ value fp8
 
 constexpr int kAbsRows = 512;

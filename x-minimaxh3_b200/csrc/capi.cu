@@ -199,6 +199,22 @@ int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride
   return cuda_status(h3b::launch_pool_sim_quant(a, st(stream)), "pool_sim_quant");
 }
 
+int h3b_qk_rmsnorm_rope(void* qkv, int64_t L, int64_t H, int64_t row_stride, int64_t q_offset, int64_t k_offset,
+                        const void* q_weight, const void* k_weight, const void* cos_table, const void* sin_table,
+                        int rot_dim, float eps, void* stream) {
+  if (L == 0) return ok();
+  if (!qkv || !q_weight || !k_weight || !cos_table || !sin_table) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (L < 0 || H <= 0 || rot_dim < 8 || rot_dim > 128 || rot_dim % 8)
+    return fail(H3B_ERR_UNSUPPORTED, "qk_rmsnorm_rope: rot_dim must be a multiple of 8 in [8, 128]");
+  if (row_stride % 4 || q_offset % 4 || k_offset % 4 || q_offset + H * 128 > row_stride ||
+      k_offset + H * 128 > row_stride)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "qk_rmsnorm_rope: bad offsets or stride");
+  h3b::QkRopeArgs a{static_cast<uint16_t*>(qkv), L, row_stride, q_offset, k_offset, (int)H, rot_dim,
+                    static_cast<const uint16_t*>(q_weight), static_cast<const uint16_t*>(k_weight),
+                    static_cast<const uint16_t*>(cos_table), static_cast<const uint16_t*>(sin_table), eps};
+  return cuda_status(h3b::launch_qk_rmsnorm_rope(a, st(stream)), "qk_rmsnorm_rope");
+}
+
 int h3b_value_fp8(const void* v, int64_t L, int64_t H, int64_t v_row_stride, int64_t Lpad, void* vt, void* vscale,
                   void* stream) {
   if (L <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "L and H must be positive");

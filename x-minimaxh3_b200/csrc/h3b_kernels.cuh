@@ -57,6 +57,17 @@ struct PoolArgs {
   float* scale;          // [H, nb]
 };
 cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s);
+struct QkRopeArgs {
+  uint16_t* x;            // bf16 rows [L, stride], q at column q_off, k at k_off (in place)
+  int64_t L, stride, q_off, k_off;
+  int H, rot_dim;
+  const uint16_t* qw;     // bf16 [128]
+  const uint16_t* kw;     // bf16 [128]
+  const uint16_t* cos_t;  // bf16 [L, rot_dim/2]
+  const uint16_t* sin_t;  // bf16 [L, rot_dim/2]
+  float eps;
+};
+cudaError_t launch_qk_rmsnorm_rope(const QkRopeArgs& a, cudaStream_t s);
 cudaError_t launch_value_fp8(const void* v, int64_t L, int64_t H, int64_t stride, int64_t Lpad, void* vt,
                              void* vscale, cudaStream_t s);
 

@@ -59,6 +59,8 @@ _SIGNATURES = {
     "h3b_key_mean": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
     "h3b_pool_sim_quant": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p, c_int64, c_void_p],
+    "h3b_qk_rmsnorm_rope": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                            c_void_p, c_int, c_float, c_void_p],
     "h3b_value_fp8": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "h3b_block_mask": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                        ctypes.POINTER(MaskParams), c_void_p, c_void_p],
@@ -93,7 +95,23 @@ def lib():
     return _lib
 
 
+# kernels each entry launches (for the benchmark's launch count); default 1
+_KERNELS_PER_CALL = {"value_fp8": 3, "key_mean": 2}
+_launches = 0
+
+
+def reset_launch_count() -> None:
+    global _launches
+    _launches = 0
+
+
+def launch_count() -> int:
+    return _launches
+
+
 def check(status: int, what: str) -> None:
+    global _launches
+    _launches += _KERNELS_PER_CALL.get(what, 1)
     if status != 0:
         msg = lib().h3b_last_error().decode(errors="replace")
         raise H3BError(f"{what} failed with status {status}: {msg}")

@@ -140,6 +140,28 @@ def rms_adaln_quantize_int8(x: torch.Tensor, norm_weight: torch.Tensor, scale: t
     return q, s
 
 
+def qk_rmsnorm_rope_(qkv: torch.Tensor, heads: int, q_offset: int, k_offset: int, q_weight: torch.Tensor,
+                     k_weight: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
+                     eps: float = 1e-6) -> torch.Tensor:
+    """In-place per-head RMSNorm + split-half partial RoPE of the Q and K heads of
+    projection rows qkv [L, W] (bf16); cos/sin tables bf16 [L, rot_dim/2]
+    (model/layers.py:72-149)."""
+    _cuda("qk_rmsnorm_rope_", qkv, q_weight, k_weight, cos_table, sin_table)
+    if qkv.dtype != torch.bfloat16 or qkv.ndim != 2 or qkv.stride(1) != 1:
+        raise ValueError("qkv must be bfloat16 rows [L, W] with unit column stride")
+    L = qkv.shape[0]
+    rot = 2 * cos_table.shape[-1]
+    if cos_table.shape != (L, rot // 2) or sin_table.shape != cos_table.shape:
+        raise ValueError("rotation tables must be [L, rot_dim/2]")
+    qw = q_weight.to(torch.bfloat16).contiguous()
+    kw = k_weight.to(torch.bfloat16).contiguous()
+    ct = cos_table.to(torch.bfloat16).contiguous()
+    st = sin_table.to(torch.bfloat16).contiguous()
+    check(lib().h3b_qk_rmsnorm_rope(_p(qkv), L, heads, qkv.stride(0), q_offset, k_offset, _p(qw), _p(kw), _p(ct),
+                                    _p(st), rot, float(eps), _stream(qkv)), "qk_rmsnorm_rope_")
+    return qkv
+
+
 # ----------------------------------------------------------------------------- GEMM
 
 
