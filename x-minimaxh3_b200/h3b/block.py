@@ -26,6 +26,7 @@ import torch
 
 from . import attention as A
 from . import ops
+from . import parallel as P
 
 
 @dataclass
@@ -121,25 +122,6 @@ class DiTBlockB200:
         return torch.addmm(self.ada_b.float(), self.ada_w.float(), t.float().reshape(-1, 1).to(self.device)
                            ).reshape(6, -1).to(torch.bfloat16)
 
-    def _alltoall_tokens_to_heads(self, qkv: torch.Tensor) -> torch.Tensor:
-        """[L/P, 3*H*D] (this rank's tokens, all heads) -> [L, 3*(H/P)*D] (all tokens, this rank's heads)."""
-        P, cfg = self.world, self.cfg
-        Lp = qkv.shape[0]
-        hd = cfg.heads // P * cfg.head_dim
-        send = qkv.view(Lp, 3, P, hd).permute(2, 0, 1, 3).contiguous()       # [P, Lp, 3, hd]
-        recv = torch.empty_like(send)
-        torch.distributed.all_to_all_single(recv, send, group=self.group)
-        return recv.view(P * Lp, 3 * hd)
-
-    def _alltoall_heads_to_tokens(self, o: torch.Tensor, Lp: int) -> torch.Tensor:
-        """[L, (H/P)*D] -> [L/P, H*D]."""
-        P = self.world
-        send = o.contiguous()                                                  # [P*Lp, hd] = [P][Lp][hd]
-        recv = torch.empty_like(send)
-        torch.distributed.all_to_all_single(recv, send, group=self.group)
-        hd = o.shape[1]
-        return recv.view(P, Lp, hd).permute(1, 0, 2).reshape(Lp, P * hd)
-
     def attention(self, qkv_heads: torch.Tensor) -> torch.Tensor:
         """qkv_heads: [L, 3*h*128] -> o [L, h, 128] (h heads of this rank)."""
         cfg = self.cfg
@@ -165,8 +147,8 @@ class DiTBlockB200:
         ops.qk_rmsnorm_rope_(qkv, cfg.heads, 0, D, self.q_norm, self.k_norm, rope[0], rope[1], cfg.qk_eps)
         Lp = x.shape[0]
         if self.world > 1:
-            o = self.attention(self._alltoall_tokens_to_heads(qkv))
-            o2 = self._alltoall_heads_to_tokens(o.view(o.shape[0], -1), Lp)
+            o = self.attention(P.tokens_to_heads(qkv, cfg.heads, cfg.head_dim, self.group))
+            o2 = P.heads_to_tokens(o.view(o.shape[0], -1), Lp, self.group)
         else:
             o2 = self.attention(qkv).view(Lp, D)
         oq, os_ = ops.quantize_int8_rowwise_convrot64(o2, cfg.convrot)
