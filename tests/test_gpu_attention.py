@@ -219,3 +219,24 @@ def test_backends_are_attention_callables(attn):
 def test_no_device_timeouts_recorded(attn):
     from h3b import device_status
     assert device_status(0) == 0
+
+
+def test_long_sequence_protocol_matches_whole_sequence(attn):
+    """Prepared K/V + query chunks reproduce the one-shot backend (same kernels,
+    same blocks) -- the streamed protocol of model/layers.py:341-356."""
+    q, k, v = qkv(1024 + 256, 2, seed=17)
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    backend = attn.SpargeLongSequenceB200(attn.MaskConfig("topk", 0.5))
+    vt, vs, L, Lpad, H = backend.prepare_long_sequence_values(vc)
+    prepared = backend.prepare_long_sequence_keys(kc, vt, vs)
+    whole = backend.long_sequence_all_queries(qc, prepared)
+    one_shot = attn.SpargeAttentionB200(attn.MaskConfig("topk", 0.5))(qc, kc, vc)
+    assert torch.equal(whole, one_shot)
+    # a 128-aligned chunk sees the same pooled query blocks -> same rows
+    chunk = backend.long_sequence_video_queries(qc[512:1024], prepared, protected_tokens=0,
+                                                query_token_indices=torch.arange(512, 1024, device="cuda"))
+    assert torch.equal(chunk, whole[512:1024])
+    dense = attn.DenseLongSequenceB200()
+    prep_d = dense.prepare_long_sequence_keys(kc, vt, vs)
+    assert torch.equal(dense.long_sequence_prefix_queries(qc[:256], prep_d),
+                       attn.SageAttentionB200()(qc, kc, vc)[:256])

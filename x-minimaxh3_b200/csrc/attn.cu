@@ -2,9 +2,15 @@
 // driven by a Sparge block bitmap.
 //
 //   S = Q_i8 . K_i8^T   tcgen05.mma kind::i8, int32 in tensor memory
-//   P = exp2((S * qs * ks * scale * log2 e) - running max) * 448 -> E4M3 (shared)
-//   O += P . V          tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32, tensor memory)
-//   out = O / rowsum * v_scale[d] -> bf16
+//   P = exp2(S * qs * ks * scale * log2 e - m) * 112 -> E4M3 (shared memory);
+//       exp2 runs on packed f16 pairs (ex2.approx.f16x2: two exponentials per
+//       MUFU op; f16 is far finer than the E4M3 result), m is a lazily updated
+//       running max: it moves only when a tile's max exceeds it by more than
+//       kTau = 2, so P <= 2^kTau * 112 = 448 (the E4M3 maximum) and the O
+//       rescale in tensor memory is rare
+//   [O | l] += P . [V | 1]   tcgen05.mma kind::f8f6f4, N = 144: the 16 extra
+//       columns of ones give the row sum of exactly the E4M3 P that meets V
+//   out = O / l * v_scale[d] -> bf16
 //
 // One CTA per (128-query tile, head), 192 threads:
 //   warp 0      TMA producer: the Q tile once, then K/V for each PAIR of selected
@@ -16,7 +22,7 @@
 //               TMEM, per-block dequant scales, online max / sum, P to shared
 //               memory in the 128-byte-swizzled K-major layout the MMA reads,
 //               O row rescale in TMEM when the max moves, final normalisation.
-// TMEM: S0 cols 0..127, S1 128..255, O 256..383.  Blocks are visited in
+// TMEM: S0 cols 0..127, S1 128..255, [O | l] 256..399.  Blocks are visited in
 // ascending order; a trailing unpaired block uses N = 64 / K = 64 MMAs.
 #include "h3b_kernels.cuh"
 
@@ -26,13 +32,18 @@ constexpr int kAttnThreads = 192;
 constexpr int kKVStages = 3;
 constexpr int kQBytes = 128 * 128;
 constexpr int kPBytes = 128 * 128;
-constexpr int kKVBytes = 32768;  // K pair 16 KB + V pair 16 KB
+// K pair 16 KB, then per V block an [128 x 64 B] tile followed by a 1 KB block
+// of E4M3 ones (16 rows): the P.V MMA reads 144 rows = V^T plus the ones.
+constexpr int kVTile = 8192 + 1024;
+constexpr int kKVBytes = 16384 + 2 * kVTile;
 constexpr int kOffQ = 0;
 constexpr int kOffP = kOffQ + kQBytes;            // 2 buffers
 constexpr int kOffKV = kOffP + 2 * kPBytes;
 constexpr int kOffBar = kOffKV + kKVStages * kKVBytes;
 constexpr int kAttnSmem = kOffBar + 256 + 1024;
-constexpr float kLog2_448 = 8.807354922057604f;
+constexpr float kLog2_112 = 6.807354922057604f;
+constexpr float kTau = 2.0f;
+constexpr int kON = 144;  // O columns incl. the row-sum block
 
 
 // Ascending walk over the K blocks of one query tile.
@@ -69,6 +80,23 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// two floats -> packed f16 pair (lo in bits 0..15), round to nearest
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+// packed f16 pair -> two E4M3 bytes (satfinite, round to nearest even), lo byte = lo half
+__device__ __forceinline__ uint32_t f16x2_to_e4m3x2(uint32_t x) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(x));
+  return (uint32_t)r;
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -85,8 +113,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_full = kv_empty + kKVStages;  // 2
   uint64_t* s_free = s_full + 2;            // 2
   uint64_t* p_full = s_free + 2;            // 2
-  uint64_t* pv_done = p_full + 2;           // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  uint64_t* pv_done = p_full + 2;           // 2 (one per P buffer)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,10 +131,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s_free[b], 128);
       mbar_init(&p_full[b], 128);
     }
-    mbar_init(pv_done, 1);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
+  // constant E4M3 ones after every V tile (never overwritten by TMA)
+  for (int i = threadIdx.x; i < kKVStages * 2 * 64; i += blockDim.x) {
+    const int st = i / 128, blk = (i / 64) & 1, w = i & 63;
+    reinterpret_cast<uint4*>(smem + kOffKV + st * kKVBytes + 16384 + blk * kVTile + 8192)[w] =
+        make_uint4(0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u);
+  }
+  fence_proxy_async_smem();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -142,7 +178,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_2d(vst, &tmV, &kv_full[stage], j0 * 64, h * 128);
         if (j1 >= 0) {
           tma_load_2d(kst + 8192, &tmK, &kv_full[stage], 0, (int)(h * a.Lkpad + (int64_t)j1 * 64));
-          tma_load_2d(vst + 8192, &tmV, &kv_full[stage], j1 * 64, h * 128);
+          tma_load_2d(vst + kVTile, &tmV, &kv_full[stage], j1 * 64, h * 128);
         }
         if (++stage == kKVStages) { stage = 0; phase ^= 1; }
       }
@@ -154,7 +190,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int stage = 0, prev_stage = 0, i = 0;
       uint32_t phase = 0;
       bool prev_has1 = false;
-      constexpr uint32_t idesc_pv = idesc_e4m3(128, 128);
+      constexpr uint32_t idesc_pv = idesc_e4m3(128, kON);
       auto issue_pv = [&](int pi) -> bool {
         const int pb = pi & 1;
         if (!mbar_wait(&p_full[pb], (uint32_t)((pi >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
@@ -164,10 +200,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int ksteps = prev_has1 ? 4 : 2;
         for (int k = 0; k < ksteps; ++k) {
           const uint64_t pd = sdesc_kmajor_sw128(pbase + 32 * k);
-          const uint64_t vd = sdesc_kmajor_sw64(vbase + (k >> 1) * 8192 + (k & 1) * 32);
+          const uint64_t vd = sdesc_kmajor_sw64(vbase + (k >> 1) * kVTile + (k & 1) * 32);
           mma_f8_ss(tmem + 256, pd, vd, idesc_pv, (pi > 0 || k > 0) ? 1u : 0u);
         }
-        mma_commit(pv_done);
+        mma_commit(&pv_done[pb]);
         mma_commit(&kv_empty[prev_stage]);
         return true;
       };
@@ -206,7 +242,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const bool row_ok = qrow < a.Lq;
     const float qs = row_ok ? __ldg(a.q_scale + (int64_t)h * a.nqs + qrow / a.q_block) : 0.f;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    float m = -__int_as_float(0x7f800000), l = 0.f;
+    const uint32_t o_addr = tmem + lane_off + 256;
+    float m = -__int_as_float(0x7f800000);
     int i = 0;
     bool ok = true;
     while (true) {
@@ -236,74 +273,82 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
       const int n0 = (int)min((int64_t)64, a.Lk - (int64_t)j0 * 64);
       const int n1 = has1 ? (int)min((int64_t)64, a.Lk - (int64_t)j1 * 64) : 0;
+      const bool full = n0 == 64 && (!has1 || n1 == 64);
       const float c0 = qs * __ldg(a.k_scale + (int64_t)h * a.Kb + j0) * a.scale_log2;
       const float c1 = has1 ? qs * __ldg(a.k_scale + (int64_t)h * a.Kb + j1) * a.scale_log2 : 0.f;
+      // tile max on the raw int32 scores (scales are positive)
       int mx0 = INT_MIN, mx1 = INT_MIN;
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c)
-        if (c < n0) mx0 = max(mx0, (int)s[c]);
-      if (has1) {
+        for (int c = 0; c < 64; ++c) mx0 = max(mx0, (int)s[c]);
+        if (has1) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) mx1 = max(mx1, (int)s[64 + c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c < n0) mx0 = max(mx0, (int)s[c]);
 #pragma unroll
         for (int c = 0; c < 64; ++c)
           if (c < n1) mx1 = max(mx1, (int)s[64 + c]);
       }
-      const float ninf = -__int_as_float(0x7f800000);
       float tmax = (float)mx0 * c0;
       if (n1 > 0) tmax = fmaxf(tmax, (float)mx1 * c1);
-      const float m_new = fmaxf(m, tmax);
-      const float base = m_new == ninf ? 0.f : m_new;
-      const float alpha = ex2(m - base);
-      // float(S) = as_float(S + 0x4B400000) - 12582912 for |S| < 2^22; fold the
-      // subtraction into the FMA constant.
-      const float off = kLog2_448 - base;
+      // lazy running max: move it only when this tile exceeds it by more than kTau
+      const bool move = tmax > m + kTau;
+      const float m_new = move ? tmax : m;
+      const bool rescale = move && i > 0;
+      const float alpha = ex2(m - m_new);
+      // x = S*c + log2(112) - m, with float(S) = as_float(S + 0x4B400000) - 12582912
+      const float off = kLog2_112 - m_new;
       const float o0 = off - 12582912.0f * c0, o1 = off - 12582912.0f * c1;
-      float sum = 0.f;
+      const int ncols = has1 ? 128 : 64;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p = c < n0 ? ex2(fmaf(__int_as_float((int)s[c] + 0x4B400000), c0, o0)) : 0.f;
-        s[c] = __float_as_uint(p);
-        sum += p;
-      }
-      if (has1) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p = c < n1 ? ex2(fmaf(__int_as_float((int)s[64 + c] + 0x4B400000), c1, o1)) : 0.f;
-          s[64 + c] = __float_as_uint(p);
-          sum += p;
-        }
-      }
-      l = l * alpha + sum;
-
-      if (i >= 1) {
-        if (!mbar_wait(pv_done, (uint32_t)((i - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
-        tc_fence_after();
-        if (alpha < 1.0f) {
-#pragma unroll 1
-          for (int c = 0; c < 128; c += 16) {
-            uint32_t o[16];
-            tmem_ld16(tmem + lane_off + 256 + c, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st16(tmem + lane_off + 256 + c, o);
+      for (int c = 0; c < 128; c += 2) {
+        if (c < ncols) {
+          const float cc = c < 64 ? c0 : c1, oo = c < 64 ? o0 : o1;
+          const float x0 = fmaf(__int_as_float((int)s[c] + 0x4B400000), cc, oo);
+          const float x1 = fmaf(__int_as_float((int)s[c + 1] + 0x4B400000), cc, oo);
+          uint32_t e = ex2_f16x2(pack_f16x2(x0, x1));
+          if (!full) {
+            const int lim = c < 64 ? n0 : n1, cl = c & 63;
+            if (cl >= lim) e &= 0xffff0000u;   // low half: column c (f16 +0 after masking)
+            if (cl + 1 >= lim) e &= 0x0000ffffu;
           }
-          tmem_wait_st();
+          s[c >> 1] = e;   // packed f16 pair, reuses the first half of s[]
         }
+      }
+
+      if (rescale) {
+        if (!mbar_wait(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
+                       H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < kON; c += 16) {
+          uint32_t o[16];
+          tmem_ld16(o_addr + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st16(o_addr + c, o);
+        }
+        tmem_wait_st();
+      }
+      // P buffer b was last read by PV(i - 2)
+      if (i >= 2 && !mbar_wait(&pv_done[b], (uint32_t)(((i - 2) >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+        ok = false;
+        break;
       }
       // P row -> shared memory, K-major, 128-byte swizzle (chunk c at c ^ (r & 7))
       uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
-      const int nchunks = has1 ? 8 : 4;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        if (c < nchunks) {
+        if (c < (ncols >> 4)) {
           uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float* pv = reinterpret_cast<const float*>(&s[16 * c + 4 * e]);
-            const uint32_t lo = f32x2_to_e4m3x2(pv[0], pv[1]);
-            const uint32_t hi = f32x2_to_e4m3x2(pv[2], pv[3]);
-            w[e] = lo | (hi << 16);
-          }
+          for (int e = 0; e < 4; ++e)
+            w[e] = f16x2_to_e4m3x2(s[8 * c + 2 * e]) | (f16x2_to_e4m3x2(s[8 * c + 2 * e + 1]) << 16);
           *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
@@ -313,16 +358,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       m = m_new;
       ++i;
     }
-    // epilogue
+    // epilogue: O / l * v_scale, l from the ones columns
     uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128;
     if (ok && i >= 1) {
-      if (mbar_wait(pv_done, (uint32_t)((i - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+      if (mbar_wait(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         tc_fence_after();
+        uint32_t lsum[16];
+        tmem_ld16(o_addr + 128, lsum);
+        tmem_wait_ld();
+        const float l = __uint_as_float(lsum[0]);
         const float inv_l = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll 1
         for (int c = 0; c < 128; c += 16) {
           uint32_t o[16];
-          tmem_ld16(tmem + lane_off + 256 + c, o);
+          tmem_ld16(o_addr + c, o);
           tmem_wait_ld();
           uint32_t packed[8];
 #pragma unroll

@@ -229,3 +229,92 @@ class SpargeAttentionB200:
         pq = prepare_queries(q, 128, self.similarity_threshold)
         bitmap = block_mask(pq, pk, self.mask)
         return attention(pq, pk, pv, bitmap)
+
+
+# ----------------------------------------------------------------------------- long-sequence protocol
+
+
+@dataclass
+class PreparedLongSequenceKVB200:
+    """Reusable quantized K/V of one layer for query-streamed attention
+    (the role of PreparedLongSequenceKV, model/kernels.py:2452-2476)."""
+
+    keys: PreparedBlocks
+    key_mean: torch.Tensor | None
+    values: PreparedValues
+    heads: int
+    key_tokens: int
+    head_dim: int = HEAD_DIM
+    tensor_layout: str = "NHD"
+
+
+def _as_lhd(x: torch.Tensor) -> torch.Tensor:
+    if x.ndim == 4:
+        if x.shape[0] != 1:
+            raise ValueError("long-sequence tensors must have batch one")
+        x = x[0]
+    return x
+
+
+class _LongSequenceMixin:
+    """Duck-typed long-sequence protocol of the native engine
+    (model/layers.py:341-356; model/kernels.py:3357-4000, 5441-5619): K/V are
+    prepared once, query chunks are evaluated against them."""
+
+    long_sequence_kv_layout = "NHD"
+    long_sequence_value_dtype = torch.bfloat16
+    supports_direct_nhd_kv = True
+
+    def resolve_long_sequence_backend(self, query_tokens: int):
+        return self
+
+    def prepare_long_sequence_values(self, value: torch.Tensor):
+        pv = prepare_values(_as_lhd(value))
+        return pv.vt, pv.scale, pv.tokens, pv.padded, pv.vt.shape[0]
+
+    def prepare_long_sequence_keys(self, key: torch.Tensor, value_fp8: torch.Tensor, value_scale: torch.Tensor,
+                                   ) -> PreparedLongSequenceKVB200:
+        key = _as_lhd(key)
+        pk, mean = prepare_keys(key, getattr(self, "similarity_threshold", -0.1),
+                                smooth=getattr(self, "smooth_k", True))
+        L = key.shape[0]
+        pv = PreparedValues(value_fp8, value_scale, L, value_fp8.shape[-1])
+        return PreparedLongSequenceKVB200(pk, mean, pv, key.shape[1], L)
+
+    def long_sequence_prefix_queries(self, query: torch.Tensor, prepared: PreparedLongSequenceKVB200) -> torch.Tensor:
+        """Protected prefix queries (text / audio): dense over every key."""
+        pq = prepare_queries(_as_lhd(query), 128, getattr(self, "similarity_threshold", -0.1))
+        return attention(pq, prepared.keys, prepared.values)
+
+    def long_sequence_all_queries(self, query: torch.Tensor, prepared: PreparedLongSequenceKVB200) -> torch.Tensor:
+        return self.long_sequence_video_queries(query, prepared, protected_tokens=0, query_token_indices=None)
+
+
+class DenseLongSequenceB200(_LongSequenceMixin, SageAttentionB200):
+    """Dense backend with the long-sequence protocol (role of
+    DenseLongSequenceAttentionBackend, model/kernels.py:5441-5619)."""
+
+    def long_sequence_video_queries(self, query, prepared, *, protected_tokens=0, query_token_indices=None):
+        pq = prepare_queries(_as_lhd(query), self.q_block)
+        return attention(pq, prepared.keys, prepared.values)
+
+
+class SpargeLongSequenceB200(_LongSequenceMixin, SpargeAttentionB200):
+    """Sparge backend with the long-sequence protocol (role of
+    SplitModalityProtectedSpargeAttentionBackend.long_sequence_video_queries,
+    model/kernels.py:3668-3997): the chunk's queries are pooled and selected
+    against the prepared keys; the protected prefix keys stay dense."""
+
+    smooth_k = True
+
+    def long_sequence_video_queries(self, query, prepared, *, protected_tokens=0, query_token_indices=None):
+        q = _as_lhd(query)
+        if query_token_indices is not None and query_token_indices.numel() != q.shape[0]:
+            raise ValueError("long-sequence Query indices must align with the chunk")
+        pq = prepare_queries(q, 128, self.similarity_threshold)
+        cfg = MaskConfig(**{**self.mask.__dict__, "protected_tokens": int(protected_tokens)})
+        if query_token_indices is not None and cfg.temporal_radius >= 0:
+            # the temporal rail assumes the whole video sequence as queries
+            cfg.temporal_radius = -1
+        bitmap = block_mask(pq, prepared.keys, cfg)
+        return attention(pq, prepared.keys, prepared.values, bitmap)
