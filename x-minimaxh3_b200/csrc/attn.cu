@@ -252,9 +252,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int j1 = it.next();
       const bool has1 = j1 >= 0;
       const int b = i & 1;
-      if (!mbar_wait(&s_full[b], (uint32_t)((i >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[b], (uint32_t)((i >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t s[128];
+      __syncwarp();
       {
         uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
         uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
@@ -298,7 +302,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // lazy running max: move it only when this tile exceeds it by more than kTau
       const bool move = tmax > m + kTau;
       const float m_new = move ? tmax : m;
-      const bool rescale = move && i > 0;
+      // tcgen05.ld / st are warp-collective: rescale the whole warp's rows when any
+      // lane needs it (lanes whose max did not move scale by exactly 1)
+      const bool rescale = __any_sync(0xffffffffu, move && i > 0);
       const float alpha = ex2(m - m_new);
       // x = S*c + log2(112) - m, with float(S) = as_float(S + 0x4B400000) - 12582912
       const float off = kLog2_112 - m_new;
@@ -321,9 +327,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
 
       if (rescale) {
-        if (!mbar_wait(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
-                       H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
+        if (!mbar_wait_warp(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
+                            H3B_STATUS_ATTN_TIMEOUT)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
+        __syncwarp();
 #pragma unroll 1
         for (int c = 0; c < kON; c += 16) {
           uint32_t o[16];
@@ -336,7 +346,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_wait_st();
       }
       // P buffer b was last read by PV(i - 2)
-      if (i >= 2 && !mbar_wait(&pv_done[b], (uint32_t)(((i - 2) >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+      if (i >= 2 &&
+          !mbar_wait_warp(&pv_done[b], (uint32_t)(((i - 2) >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         ok = false;
         break;
       }
@@ -361,8 +372,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // epilogue: O / l * v_scale, l from the ones columns
     uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128;
     if (ok && i >= 1) {
-      if (mbar_wait(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+      if (mbar_wait_warp(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
+                         H3B_STATUS_ATTN_TIMEOUT)) {
         tc_fence_after();
+        __syncwarp();
         uint32_t lsum[16];
         tmem_ld16(o_addr + 128, lsum);
         tmem_wait_ld();
@@ -394,6 +407,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

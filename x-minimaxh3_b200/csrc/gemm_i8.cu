@@ -206,8 +206,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       const int mb = t / num_n, nb = t % num_n;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
       tc_fence_after();
+      __syncwarp();
       const int m = mb * kBM + row_in_tile;
       const float xs_m = (KIND != kEpiInt32 && m < a.M) ? __ldg(a.xs + m) : 0.0f;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
@@ -230,6 +231,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }

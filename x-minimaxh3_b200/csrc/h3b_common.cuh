@@ -127,20 +127,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait.  `abort_flag` (shared) lets the other roles of a CTA give up at
-// once after the first timeout.  Returns false on timeout or abort.
+// once after the first timeout.  Two independent bounds: wall clock (%globaltimer)
+// and a try count, so the wait ends even if the timer were not to advance.
+// Returns false on timeout or abort.
+constexpr uint32_t kWaitMaxTries = 1u << 26;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  while (true) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t n = 0;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (n >= kWaitMaxTries || globaltimer_ns() - t0 > kWaitLimitNs) {
       *abort_flag = 1;
       record_status(code);
       return false;
     }
   }
+}
+// Warp-wide bounded wait: every lane waits, then the warp agrees on the outcome,
+// so warp-collective (.sync.aligned) instructions after it run converged.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               int code) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, code);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ------------------------------------------------------------------ TMA (no multicast)
