@@ -59,7 +59,7 @@ int h3b_device_status(int device, int* status, int reset);
 /* Per-row dynamic INT8 quantization: scale[r] = max(|x[r,:]|)/127 (at least
  * 1e-30), q = rint(bf16(x / bf16(scale))) clamped to [-128, 127].
  * x: bf16 [rows, x_row_stride] (first `cols` columns used), q: int8 [rows, cols],
- * scales: f32 [rows].  cols % 16 == 0, cols <= 32768.
+ * scales: f32 [rows].  cols % 16 == 0, cols <= 16384.
  * Replaces launch_quantize_int8_rowwise_kernel
  * (comfy_kitchen backends/cuda/ops/int8_linear.cu:1035-1084). */
 int h3b_quantize_int8_rowwise(const void* x, int64_t rows, int64_t cols, int64_t x_row_stride, void* q,
@@ -69,7 +69,7 @@ int h3b_quantize_int8_rowwise(const void* x, int64_t rows, int64_t cols, int64_t
  * every 256-column group, fp32) + per-row INT8 quantization.
  * input_act: 0 none, 1 gelu_tanh, 2 swiglu (x row = [gate | up], 2*cols wide).
  * x: bf16 [rows, x_row_stride]; q: int8 [rows, cols]; scales: f32 [rows].
- * group_size must be 256; cols % 256 == 0, cols <= 32768.
+ * group_size must be 256; cols % 256 == 0, cols <= 16384.
  * Replaces launch_quantize_int8_rowwise_convrot64 / _convrot_kernel
  * (int8_linear.cu:1086-1160, 1294-1408). */
 int h3b_quantize_int8_rowwise_convrot(const void* x, int64_t rows, int64_t cols, int64_t x_row_stride,

@@ -269,11 +269,11 @@ float h3bo_tree_sum(const float* v, int n) {
 }
 
 /* Threads per row used by the CUDA quantizer: K/16 chunks of 16 columns,
- * rounded up to a warp multiple, at most 1024 (thread t owns chunks t, t+T, ...). */
+ * rounded up to a warp multiple, at most 512 (thread t owns chunks t, t+T, ...). */
 int h3bo_quant_threads(int64_t K) {
     int64_t chunks = K / 16;
     int64_t T = (chunks + 31) / 32 * 32;
-    return (int)(T > 1024 ? 1024 : T);
+    return (int)(T > 512 ? 512 : T);
 }
 
 /* RMSNorm(weight) followed by AdaLN modulation with bf16 materialization after

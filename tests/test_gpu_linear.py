@@ -32,7 +32,7 @@ def _x(m, k, seed=0):
     return outlier_activations(g, m, k).to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("m,k", [(1, 256), (77, 512), (300, 4096), (5, 5376), (3, 16384), (2, 32768), (9, 48)])
+@pytest.mark.parametrize("m,k", [(1, 256), (77, 512), (300, 4096), (5, 5376), (3, 16384), (2, 14336), (9, 48)])
 def test_quant_rowwise_bit_exact(ops, m, k):
     x = _x(m, k, seed=m + k)
     q, s = ops.quantize_int8_rowwise(x.cuda())
@@ -49,7 +49,7 @@ def test_quant_rowwise_golden_edge_rows(ops):
 
 
 @pytest.mark.parametrize("act", [None, "gelu_tanh", "swiglu"])
-@pytest.mark.parametrize("m,k", [(1, 256), (130, 4096), (7, 5376), (4, 14336), (3, 16384), (2, 28672)])
+@pytest.mark.parametrize("m,k", [(1, 256), (130, 4096), (7, 5376), (4, 14336), (3, 16384), (1000, 8192)])
 def test_quant_convrot_bit_exact(ops, act, m, k):
     width = 2 * k if act == "swiglu" else k
     x = _x(m, width, seed=3 * m + k)
@@ -76,7 +76,7 @@ def test_rms_adaln_quant_bit_exact(ops, convrot, m, k):
     w = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
     sc = (0.2 * torch.randn(3, k, generator=g)).to(torch.bfloat16)
     sh = (0.2 * torch.randn(3, k, generator=g)).to(torch.bfloat16)
-    segs = ((0, m // 3, 2), (m // 3, m // 2, 0), (m // 2, m, 1)) if m >= 3 else ((0, m, 1),)
+    segs = ((0, m // 4, 2), (m // 4, m // 2, 0), (m // 2, m, 1)) if m >= 8 else ((0, m, 1),)
     q, s = ops.rms_adaln_quantize_int8(x.cuda(), w.cuda(), sc.cuda(), sh.cuda(), segs, 1e-5, convrot)
     seg_row = ops.segment_rows(segs, m, "cpu")
     qo, so = O.rms_adaln_quant(bits(x), bits(w), bits(sc), bits(sh),

@@ -55,8 +55,8 @@ int h3b_quantize_int8_rowwise(const void* x, int64_t rows, int64_t cols, int64_t
                               void* stream) {
   if (rows == 0 || cols == 0) return ok();
   if (!x || !q || !scales) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
-  if (rows < 0 || cols < 0 || cols % 16 || cols > 32768 || x_row_stride < cols || x_row_stride % 8)
-    return fail(H3B_ERR_UNSUPPORTED, "quantize_int8_rowwise: need cols % 16 == 0, cols <= 32768, stride % 8 == 0");
+  if (rows < 0 || cols < 0 || cols % 16 || cols > 16384 || x_row_stride < cols || x_row_stride % 8)
+    return fail(H3B_ERR_UNSUPPORTED, "quantize_int8_rowwise: need cols % 16 == 0, cols <= 16384, stride % 8 == 0");
   if (rows > INT_MAX) return fail(H3B_ERR_UNSUPPORTED, "too many rows");
   if (!aligned16(x) || !aligned16(q)) return fail(H3B_ERR_UNSUPPORTED, "x and q must be 16-byte aligned");
   h3b::QuantArgs a{static_cast<const uint16_t*>(x), x_row_stride, (int)cols, 0, static_cast<int8_t*>(q),
@@ -71,8 +71,8 @@ int h3b_quantize_int8_rowwise_convrot(const void* x, int64_t rows, int64_t cols,
   if (group_size != 256) return fail(H3B_ERR_UNSUPPORTED, "ConvRot group size must be 256");
   if (input_act < 0 || input_act > 2) return fail(H3B_ERR_INVALID_ARGUMENT, "input_act must be 0, 1 or 2");
   const int64_t in_w = input_act == 2 ? 2 * cols : cols;
-  if (rows < 0 || cols % 256 || cols > 32768 || x_row_stride < in_w || x_row_stride % 8)
-    return fail(H3B_ERR_UNSUPPORTED, "quantize_int8_rowwise_convrot: need cols % 256 == 0, cols <= 32768");
+  if (rows < 0 || cols % 256 || cols > 16384 || x_row_stride < in_w || x_row_stride % 8)
+    return fail(H3B_ERR_UNSUPPORTED, "quantize_int8_rowwise_convrot: need cols % 256 == 0, cols <= 16384");
   if (rows > INT_MAX) return fail(H3B_ERR_UNSUPPORTED, "too many rows");
   if (!aligned16(x) || !aligned16(q)) return fail(H3B_ERR_UNSUPPORTED, "x and q must be 16-byte aligned");
   h3b::QuantArgs a{static_cast<const uint16_t*>(x), x_row_stride, (int)cols, input_act, static_cast<int8_t*>(q),
@@ -89,7 +89,7 @@ int h3b_rms_adaln_quantize_int8(const void* x, int64_t rows, int64_t cols, int64
     return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
   if (convrot_group_size != 0 && convrot_group_size != 256)
     return fail(H3B_ERR_UNSUPPORTED, "convrot_group_size must be 0 or 256");
-  if (rows < 0 || cols % (convrot_group_size ? 256 : 16) || cols > 32768 || x_row_stride < cols || x_row_stride % 8)
+  if (rows < 0 || cols % (convrot_group_size ? 256 : 16) || cols > 16384 || x_row_stride < cols || x_row_stride % 8)
     return fail(H3B_ERR_UNSUPPORTED, "rms_adaln_quantize_int8: unsupported width or stride");
   if (!aligned16(x) || !aligned16(q) || !aligned16(norm_weight) || !aligned16(scale_table) || !aligned16(shift_table))
     return fail(H3B_ERR_UNSUPPORTED, "operands must be 16-byte aligned");

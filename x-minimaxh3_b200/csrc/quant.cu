@@ -1,6 +1,7 @@
 // quant.cu -- per-token dynamic INT8 activation quantization for the DiT linears.
 //
-// One CTA per token row, T threads (a multiple of 32, at most 1024); thread t
+// Persistent CTAs of T threads (a multiple of 32, at most 512) walk the token
+// rows (the next row is loaded while the current one is processed); thread t
 // owns the 16-column chunks c = t, t+T, ... of the row, so every global access
 // is a 32-byte vector load or a 16-byte vector store.  Variants (template):
 //   * plain row quantization        (comfy_kitchen int8_linear.cu:158-200)
@@ -20,15 +21,29 @@ namespace h3b {
 enum QuantMode : int { kPlain = 0, kConvRot = 1 };
 
 
-constexpr int kMaxIters = 2;  // chunks per thread; K <= 32 * 1024
+constexpr int kMaxIters = 2;  // chunks per thread; K <= 2 * 512 * 16 = 16384
 
+// One radix-4 butterfly of the regular H4 matrix, outputs in the reference's
+// operation order (int8_linear.cu:217-250): y0 = ((x0+x1)+x2)-x3,
+// y1 = ((x0+x1)-x2)+x3, y2 = ((x0-x1)+x2)+x3, y3 = ((-x0+x1)+x2)+x3, times 1/2.
+// x0+x1 and x0-x1 are shared; (-x0+x1)+x2 == x2-(x0-x1) exactly.
 __device__ __forceinline__ void h4_stage(const float* x, int s, float* y, int base) {
   const float x0 = x[base], x1 = x[base + s], x2 = x[base + 2 * s], x3 = x[base + 3 * s];
-  y[base] = __fmul_rn(0.5f, __fsub_rn(__fadd_rn(__fadd_rn(x0, x1), x2), x3));
-  y[base + s] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(__fadd_rn(x0, x1), x2), x3));
-  y[base + 2 * s] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(__fsub_rn(x0, x1), x2), x3));
-  y[base + 3 * s] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(__fadd_rn(-x0, x1), x2), x3));
+  const float s01 = __fadd_rn(x0, x1), d01 = __fsub_rn(x0, x1);
+  y[base] = __fmul_rn(0.5f, __fsub_rn(__fadd_rn(s01, x2), x3));
+  y[base + s] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(s01, x2), x3));
+  y[base + 2 * s] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(d01, x2), x3));
+  y[base + 3 * s] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(x2, d01), x3));
 }
+// Correctly rounded a / b from rb = RN(1/b) (Markstein: q = RN(a*rb) is within
+// one ulp, the residual a - b*q is exact through one fma, and q + residual*rb
+// rounds to RN(a/b) when no underflow or overflow occurs).
+__device__ __forceinline__ float div_rn_by(float a, float b, float rb) {
+  const float q = __fmul_rn(a, rb);
+  const float r = fmaf(-q, b, a);
+  return fmaf(r, rb, q);
+}
+
 // Two radix-4 stages (stride 1 then 4) over 16 values held by one thread.
 __device__ __forceinline__ void fht16(float (&v)[16]) {
   float t[16];
@@ -98,125 +113,165 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[32];
 }
 
+// raw bf16 chunks of one row owned by this thread (prefetched one row ahead)
+struct RowRegs {
+  uint4 x[kMaxIters][2];
+  uint4 u[kMaxIters][2];  // the `up` half of a swiglu row
+};
+
+template <int ACT>
+__device__ __forceinline__ void load_row(const QuantArgs& a, int64_t row, int t, int T, int chunks, RowRegs& r) {
+  const uint16_t* xr = a.x + row * a.x_stride;
+#pragma unroll
+  for (int i = 0; i < kMaxIters; ++i) {
+    const int c = t + i * T;
+    if (c < chunks) {
+      const uint4* p = reinterpret_cast<const uint4*>(xr + c * 16);
+      r.x[i][0] = __ldg(p);
+      r.x[i][1] = __ldg(p + 1);
+      if (ACT == 2) {
+        const uint4* pu = reinterpret_cast<const uint4*>(xr + a.K + c * 16);
+        r.u[i][0] = __ldg(pu);
+        r.u[i][1] = __ldg(pu + 1);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack16(const uint4 (&w)[2], float (&v)[16]) {
+  const uint32_t q[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = __uint_as_float(q[i] << 16);
+    v[2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+  }
+}
+
+// Persistent: CTA b handles rows b, b + gridDim.x, ...; the next row's loads are
+// issued before the current row is processed.
 template <int MODE, int ACT, bool RMS>
-__global__ void __launch_bounds__(1024) quant_rows_kernel(QuantArgs a) {
+__global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t rows) {
   extern __shared__ float tile[];       // (T/16) groups x 16 x 17 floats
   __shared__ float red[33];
   const int T = blockDim.x, t = threadIdx.x;
   const int K = a.K, chunks = K >> 4;
-  const int64_t row = blockIdx.x;
-  const uint16_t* xr = a.x + row * a.x_stride;
+  float* my_tile = tile + (t >> 4) * (16 * 17);
+  const int a_idx = t & 15;  // row of the 16x16 group array owned for loads / stores
 
-  float v[kMaxIters][16];
-  bool live[kMaxIters];
+  RowRegs nxt;
+  int64_t row = blockIdx.x;
+  if (row < rows) load_row<ACT>(a, row, t, T, chunks, nxt);
+  for (; row < rows; row += gridDim.x) {
+    const RowRegs cur = nxt;
+    if (row + gridDim.x < rows) load_row<ACT>(a, row + gridDim.x, t, T, chunks, nxt);
+
+    float v[kMaxIters][16];
+    bool live[kMaxIters];
 #pragma unroll
-  for (int i = 0; i < kMaxIters; ++i) {
-    const int c = t + i * T;
-    live[i] = c < chunks;
-    if (live[i]) {
-      if (ACT == 2) {
-        float g[16], u[16];
-        load16_bf16(xr + c * 16, g);
-        load16_bf16(xr + K + c * 16, u);
+    for (int i = 0; i < kMaxIters; ++i) {
+      live[i] = t + i * T < chunks;
+      if (live[i]) {
+        unpack16(cur.x[i], v[i]);
+        if (ACT == 2) {
+          float u[16];
+          unpack16(cur.u[i], u);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[i][j] = swiglu(g[j], u[j]);
-      } else {
-        load16_bf16(xr + c * 16, v[i]);
-        if (ACT == 1) {
+          for (int j = 0; j < 16; ++j) v[i][j] = swiglu(v[i][j], u[j]);
+        } else if (ACT == 1) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[i][j] = gelu_tanh(v[i][j]);
         }
-      }
-    } else {
+      } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
+        for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
+      }
     }
-  }
 
-  if (RMS) {
-    float part = 0.0f;
+    if (RMS) {
+      float part = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kMaxIters; ++i)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part = __fadd_rn(part, __fmul_rn(v[i][j], v[i][j]));
+      const float ss = block_tree_sum(part, red);
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+      const int r = a.seg_row ? a.seg_row[row] : 0;
+      const uint16_t* sc = a.scale_tab + (int64_t)r * K;
+      const uint16_t* sh = a.shift_tab + (int64_t)r * K;
+#pragma unroll
+      for (int i = 0; i < kMaxIters; ++i) {
+        if (!live[i]) continue;
+        const int c0 = (t + i * T) * 16;
+        float w[16], s1[16], s2[16];
+        load16_bf16(a.norm_w + c0, w);
+        load16_bf16(sc + c0, s1);
+        load16_bf16(sh + c0, s2);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float n = bf16r(__fmul_rn(__fmul_rn(v[i][j], inv), w[j]));
+          n = bf16r(__fmul_rn(n, bf16r(__fadd_rn(1.0f, s1[j]))));
+          v[i][j] = bf16r(__fadd_rn(n, s2[j]));
+        }
+      }
+    }
+
+    if (MODE == kConvRot) {
+#pragma unroll
+      for (int i = 0; i < kMaxIters; ++i) {
+        if (i * T >= chunks) break;  // uniform across the block
+        fht16(v[i]);
+        __syncthreads();
+#pragma unroll
+        for (int b = 0; b < 16; ++b) my_tile[a_idx * 17 + b] = v[i][b];
+        __syncthreads();
+        // thread now takes column b = a_idx of its group
+#pragma unroll
+        for (int r = 0; r < 16; ++r) v[i][r] = my_tile[r * 17 + a_idx];
+        fht16(v[i]);
+      }
+    }
+
+    float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < kMaxIters; ++i)
+      if (live[i])
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part = __fadd_rn(part, __fmul_rn(v[i][j], v[i][j]));
-    const float ss = block_tree_sum(part, red);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-    const int r = a.seg_row ? a.seg_row[row] : 0;
-    const uint16_t* sc = a.scale_tab + (int64_t)r * K;
-    const uint16_t* sh = a.shift_tab + (int64_t)r * K;
+        for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    amax = block_max(amax, red);
+    const float scale = fmaxf(__fmul_rn(fminf(amax, 3.38953139e38f), 1.0f / 127.0f), 1.0e-30f);
+    const float st = bf16r(scale);
+    const float rst = __fdiv_rn(1.0f, st);
+    if (t == 0) a.scales[row] = scale;
+
+    int8_t* qr = a.q + row * (int64_t)K;
 #pragma unroll
     for (int i = 0; i < kMaxIters; ++i) {
-      if (!live[i]) continue;
-      const int c0 = (t + i * T) * 16;
-      float w[16], s1[16], s2[16];
-      load16_bf16(a.norm_w + c0, w);
-      load16_bf16(sc + c0, s1);
-      load16_bf16(sh + c0, s2);
+      if (i * T >= chunks) break;
+      uint32_t packed[4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float n = bf16r(__fmul_rn(__fmul_rn(v[i][j], inv), w[j]));
-        n = bf16r(__fmul_rn(n, bf16r(__fadd_rn(1.0f, s1[j]))));
-        v[i][j] = bf16r(__fadd_rn(n, s2[j]));
+      for (int w = 0; w < 4; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float s = bf16r(div_rn_by(bf16r(v[i][4 * w + j]), st, rst));
+          const float qv = fminf(127.0f, fmaxf(-128.0f, rintf(s)));
+          word |= ((uint32_t)(int)qv & 0xffu) << (8 * j);
+        }
+        packed[w] = word;
       }
-    }
-  }
-
-  float* my_tile = tile + (t >> 4) * (16 * 17);
-  const int a_idx = t & 15;  // row of the 16x16 group array owned for loads / stores
-  if (MODE == kConvRot) {
+      if (MODE == kConvRot) {
+        // codes are held by column; transpose back through shared memory
+        uint8_t* bt = reinterpret_cast<uint8_t*>(my_tile);
+        __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kMaxIters; ++i) {
-      if (i * T >= chunks) break;  // uniform across the block
-      fht16(v[i]);
-      __syncthreads();
-#pragma unroll
-      for (int b = 0; b < 16; ++b) my_tile[a_idx * 17 + b] = v[i][b];
-      __syncthreads();
-      // thread now takes column b = a_idx of its group
-#pragma unroll
-      for (int r = 0; r < 16; ++r) v[i][r] = my_tile[r * 17 + a_idx];
-      fht16(v[i]);
-    }
-  }
-
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kMaxIters; ++i)
-    if (live[i])
-#pragma unroll
-      for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
-  amax = block_max(amax, red);
-  const float scale = fmaxf(__fmul_rn(fminf(amax, 3.38953139e38f), 1.0f / 127.0f), 1.0e-30f);
-  const float st = bf16r(scale);
-  if (t == 0) a.scales[row] = scale;
-
-  int8_t* qr = a.q + row * (int64_t)K;
-#pragma unroll
-  for (int i = 0; i < kMaxIters; ++i) {
-    if (i * T >= chunks) break;
-    uint32_t packed[4];
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float s = bf16r(__fdiv_rn(bf16r(v[i][4 * w + j]), st));
-        float qv = fminf(127.0f, fmaxf(-128.0f, rintf(s)));
-        word |= ((uint32_t)(int)qv & 0xffu) << (8 * j);
+        for (int r = 0; r < 16; ++r) bt[r * 16 + a_idx] = (uint8_t)(packed[r >> 2] >> (8 * (r & 3)));
+        __syncthreads();
+        const uint4 row16 = *reinterpret_cast<const uint4*>(bt + a_idx * 16);
+        if (live[i]) *reinterpret_cast<uint4*>(qr + (t + i * T) * 16) = row16;
+      } else if (live[i]) {
+        *reinterpret_cast<uint4*>(qr + (t + i * T) * 16) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
       }
-      packed[w] = word;
-    }
-    if (MODE == kConvRot) {
-      // codes are held by column; transpose back through shared memory
-      uint8_t* bt = reinterpret_cast<uint8_t*>(my_tile);
-      __syncthreads();
-#pragma unroll
-      for (int r = 0; r < 16; ++r) bt[r * 16 + a_idx] = (uint8_t)(packed[r >> 2] >> (8 * (r & 3)));
-      __syncthreads();
-      const uint4 row16 = *reinterpret_cast<const uint4*>(bt + a_idx * 16);
-      if (live[i]) *reinterpret_cast<uint4*>(qr + (t + i * T) * 16) = row16;
-    } else if (live[i]) {
-      *reinterpret_cast<uint4*>(qr + (t + i * T) * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
   }
 }
@@ -224,7 +279,7 @@ __global__ void __launch_bounds__(1024) quant_rows_kernel(QuantArgs a) {
 int quant_threads_for(int K) {
   int chunks = K / 16;
   int T = ((chunks + 31) / 32) * 32;
-  return T > 1024 ? 1024 : T;
+  return T > 512 ? 512 : T;
 }
 
 template <int MODE, int ACT, bool RMS>
@@ -233,10 +288,18 @@ static cudaError_t launch_q(const QuantArgs& a, int64_t rows, cudaStream_t s) {
   const size_t smem = (size_t)(T / 16) * 16 * 17 * sizeof(float);
   auto k = quant_rows_kernel<MODE, ACT, RMS>;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    cudaError_t e0 = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e0 != cudaSuccess) return e0;
   }
-  k<<<(unsigned)rows, T, smem, s>>>(a);
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, T, smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t cap = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+  const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+  k<<<grid, T, smem, s>>>(a, rows);
   return cudaGetLastError();
 }
 

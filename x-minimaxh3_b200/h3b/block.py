@@ -119,8 +119,8 @@ class DiTBlockB200:
 
     # ------------------------------------------------------------------ stages
     def modulation(self, t: torch.Tensor) -> torch.Tensor:
-        return torch.addmm(self.ada_b.float(), self.ada_w.float(), t.float().reshape(-1, 1).to(self.device)
-                           ).reshape(6, -1).to(torch.bfloat16)
+        tv = t.float().reshape(-1).to(self.device)
+        return (torch.mv(self.ada_w.float(), tv) + self.ada_b.float()).reshape(6, -1).to(torch.bfloat16)
 
     def attention(self, qkv_heads: torch.Tensor) -> torch.Tensor:
         """qkv_heads: [L, 3*h*128] -> o [L, h, 128] (h heads of this rank)."""
