@@ -138,6 +138,16 @@ int64_t h3b_key_mean_workspace_bytes(int64_t L, int64_t H);
 int h3b_key_mean(const void* k, int64_t L, int64_t H, int64_t k_row_stride, void* mean, void* workspace,
                  int64_t workspace_bytes, void* stream);
 
+/* h3b_key_mean for callers that cannot allocate device memory (no counterpart
+ * in the reference, which always allocates its temporaries with torch): the
+ * same result, with the scratch taken from a fixed 8 MiB array inside the
+ * library instead of a caller workspace.  Limit: ceil(L/1024) * H * 128 <=
+ * 2^20 (e.g. L <= 262,144 at H = 32); larger calls return H3B_ERR_UNSUPPORTED.
+ * The first call on each device looks the array up (cudaGetSymbolAddress) and
+ * should come before any stream capture.  Calls share the array: calls whose
+ * kernels overlap on the GPU race; ordered calls are independent. */
+int h3b_key_mean_no_alloc(const void* k, int64_t L, int64_t H, int64_t k_row_stride, void* mean, void* stream);
+
 /* Sparge per-block preparation of Q (block 128) or K (block 64, with `mean`
  * for K mean-smoothing value = bf16(x - mean)):
  *   pooled  bf16 [H, nb, 128]  = bf16(sum(value)/valid_rows)

@@ -12,6 +12,8 @@
 //               to [H, 128, Lpad] (model/compact_fp8.py:13-300)
 // Every reduction runs in the order the CPU oracle restates, so results are
 // bit-identical to it.
+#include <mutex>
+
 #include "h3b_kernels.cuh"
 
 namespace h3b {
@@ -66,6 +68,53 @@ cudaError_t launch_key_mean(const void* k, int64_t L, int64_t H, int64_t stride,
   key_mean_final_kernel<<<(cols + 255) / 256, 256, 0, s>>>(static_cast<const double*>(ws), chunks, cols, L,
                                                              static_cast<uint16_t*>(mean));
   return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ key mean, no allocation
+
+// A variant of launch_key_mean for callers that cannot allocate device memory
+// (for example a host that hands all of the GPU's memory to its own pool and
+// cannot give this library a workspace, or code running where a device
+// allocation is not permitted).  Its scratch -- one fp64 partial sum per
+// (1024-token chunk, head, channel) -- lives in this fixed, file-scope device
+// array instead: 2^20 doubles (8 MiB), held by every GPU that loads the library
+// until the process exits.  ceil(L / 1024) * H * 128 must not exceed 2^20
+// (e.g. L <= 262,144 tokens at 32 heads).  Every call on a device shares the
+// array and nothing is cleared between calls: each call writes every partial
+// it reads before reading it, so stale contents are harmless, but two calls
+// whose kernels overlap on the GPU (different streams, no ordering) race on it.
+constexpr int64_t kKeyMeanScratchDoubles = int64_t(1) << 20;
+static __device__ __align__(256) double g_key_mean_scratch[kKeyMeanScratchDoubles];
+
+// Device address of g_key_mean_scratch, looked up once per device with that
+// device current (in host code the array's name is only a host-side stand-in).
+static std::mutex g_scratch_mu;
+static double* g_scratch_ptr[64] = {};
+
+static cudaError_t key_mean_scratch_for_current_device(double** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_key_mean_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = static_cast<double*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+int64_t key_mean_static_capacity() { return kKeyMeanScratchDoubles; }
+
+cudaError_t launch_key_mean_static(const void* k, int64_t L, int64_t H, int64_t stride, void* mean,
+                                   cudaStream_t s) {
+  double* scratch = nullptr;
+  cudaError_t e = key_mean_scratch_for_current_device(&scratch);
+  if (e != cudaSuccess) return e;
+  return launch_key_mean(k, L, H, stride, mean, scratch, s);
 }
 
 // ------------------------------------------------------------------ pool / sim / quant

@@ -183,6 +183,19 @@ int h3b_key_mean(const void* k, int64_t L, int64_t H, int64_t k_row_stride, void
   return cuda_status(h3b::launch_key_mean(k, L, H, k_row_stride, mean, workspace, st(stream)), "key_mean");
 }
 
+int h3b_key_mean_no_alloc(const void* k, int64_t L, int64_t H, int64_t k_row_stride, void* mean, void* stream) {
+  if (L <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "L and H must be positive");
+  if (!k || !mean) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (k_row_stride < H * 128) return fail(H3B_ERR_INVALID_ARGUMENT, "k_row_stride < H*128");
+  const int64_t need = h3b::key_mean_workspace(L, H) / (int64_t)sizeof(double);
+  if (need > h3b::key_mean_static_capacity())
+    return fail(H3B_ERR_UNSUPPORTED, "key_mean_no_alloc: ceil(L/1024)*H*128 = " + std::to_string(need) +
+                                         " partial sums exceed the fixed scratch of " +
+                                         std::to_string(h3b::key_mean_static_capacity()) +
+                                         "; use h3b_key_mean with a caller workspace");
+  return cuda_status(h3b::launch_key_mean_static(k, L, H, k_row_stride, mean, st(stream)), "key_mean_no_alloc");
+}
+
 int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride, const void* mean, int block,
                        const void* thr, void* pooled, void* similar, void* qi8, void* scale, int64_t Lpad,
                        void* stream) {

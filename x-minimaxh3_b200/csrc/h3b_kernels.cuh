@@ -44,6 +44,9 @@ cudaError_t launch_w4_decode(const void* qw, const void* s_rel, int s_rel_kind, 
 
 int64_t key_mean_workspace(int64_t L, int64_t H);
 cudaError_t launch_key_mean(const void* k, int64_t L, int64_t H, int64_t stride, void* mean, void* ws, cudaStream_t s);
+int64_t key_mean_static_capacity();
+cudaError_t launch_key_mean_static(const void* k, int64_t L, int64_t H, int64_t stride, void* mean,
+                                   cudaStream_t s);
 
 struct PoolArgs {
   const uint16_t* x;

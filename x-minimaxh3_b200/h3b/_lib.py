@@ -57,6 +57,7 @@ _SIGNATURES = {
                                          c_void_p],
     "h3b_key_mean_workspace_bytes": [c_int64, c_int64],
     "h3b_key_mean": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
+    "h3b_key_mean_no_alloc": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "h3b_pool_sim_quant": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p, c_int64, c_void_p],
     "h3b_qk_rmsnorm_rope": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
@@ -96,7 +97,7 @@ def lib():
 
 
 # kernels each entry launches (for the benchmark's launch count); default 1
-_KERNELS_PER_CALL = {"value_fp8": 3, "key_mean": 2}
+_KERNELS_PER_CALL = {"value_fp8": 3, "key_mean": 2, "key_mean_no_alloc": 2}
 _launches = 0
 
 
