@@ -12,23 +12,27 @@
 //       columns of ones give the row sum of exactly the E4M3 P that meets V
 //   out = O / l * v_scale[d] -> bf16
 //
-// One CTA per (128-query tile, head), 192 threads:
+// One CTA per (128-query tile, head), 320 threads:
 //   warp 0      TMA producer: the Q tile once, then K/V for each PAIR of selected
 //               64-key blocks (K: 2 x [64 x 128 B], 128-byte swizzle; V^T: 2 x
 //               [128 x 64 B], 64-byte swizzle) into a 3-stage ring; no multicast
 //   warp 1      TMEM allocator + MMA issuer: S for pair i into one of two S
 //               buffers, then O += P(i-1) . V(i-1) once the softmax published P(i-1)
-//   warps 2..5  softmax, one query row per thread (its TMEM lane): S row from
-//               TMEM, per-block dequant scales, online max / sum, P to shared
-//               memory in the 128-byte-swizzled K-major layout the MMA reads,
-//               O row rescale in TMEM when the max moves, final normalisation.
+//   warps 2..9  softmax, two warps per TMEM lane quadrant: for its 32 query rows
+//               warp 2..5 takes key columns 0..63 (block j0), warp 6..9 columns
+//               64..127 (block j1); the two exchange only their tile max per row
+//               through shared memory (named barrier per quadrant), then each
+//               writes its half of the P row (128-byte-swizzled K-major, as the
+//               MMA reads it), rescales its half of the O row in TMEM when the
+//               running max moves, and normalises its half of the output.
 // TMEM: S0 cols 0..127, S1 128..255, [O | l] 256..399.  Blocks are visited in
 // ascending order; a trailing unpaired block uses N = 64 / K = 64 MMAs.
 #include "h3b_kernels.cuh"
 
 namespace h3b {
 
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 320;
+constexpr int kSoftmaxThreads = 256;
 constexpr int kKVStages = 3;
 constexpr int kQBytes = 128 * 128;
 constexpr int kPBytes = 128 * 128;
@@ -40,7 +44,8 @@ constexpr int kOffQ = 0;
 constexpr int kOffP = kOffQ + kQBytes;            // 2 buffers
 constexpr int kOffKV = kOffP + 2 * kPBytes;
 constexpr int kOffBar = kOffKV + kKVStages * kKVBytes;
-constexpr int kAttnSmem = kOffBar + 256 + 1024;
+constexpr int kOffXchg = kOffBar + 256;            // float [2 parity][2 halves][128 rows]
+constexpr int kAttnSmem = kOffXchg + 2 * 2 * 128 * 4 + 1024;
 constexpr float kLog2_112 = 6.807354922057604f;
 constexpr float kTau = 2.0f;
 constexpr int kON = 144;  // O columns incl. the row-sum block
@@ -114,7 +119,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;            // 2
   uint64_t* p_full = s_free + 2;            // 2
   uint64_t* pv_done = p_full + 2;           // 2 (one per P buffer)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* xbar = pv_done + 2;             // 4: tile-max exchange per lane quadrant (64 threads)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,11 +134,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 128);
-      mbar_init(&p_full[b], 128);
+      mbar_init(&s_free[b], kSoftmaxThreads);
+      mbar_init(&p_full[b], kSoftmaxThreads);
     }
     mbar_init(&pv_done[0], 1);
     mbar_init(&pv_done[1], 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -235,14 +242,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (ok && i >= 1) issue_pv(i - 1);
     }
   } else {
-    // softmax warps 2..5: TMEM lane quadrant warp % 4
+    // softmax warps 2..9: TMEM lane quadrant warp % 4, key-column half (warp - 2) / 4
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int64_t qrow = (int64_t)qt * 128 + r;
     const bool row_ok = qrow < a.Lq;
     const float qs = row_ok ? __ldg(a.q_scale + (int64_t)h * a.nqs + qrow / a.q_block) : 0.f;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t o_addr = tmem + lane_off + 256;
+    float* xchg = reinterpret_cast<float*>(smem + kOffXchg);   // [parity][half][row]
+    const int o_c0 = half ? 80 : 0, o_c1 = half ? kON : 80;  // this warp's O columns (16-column chunks)
     float m = -__int_as_float(0x7f800000);
     int i = 0;
     bool ok = true;
@@ -252,53 +262,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int j1 = it.next();
       const bool has1 = j1 >= 0;
       const int b = i & 1;
+      const int jb = half ? j1 : j0;           // this warp's key block (-1: none)
+      const bool mine = jb >= 0;
       if (!mbar_wait_warp(&s_full[b], (uint32_t)((i >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s[128];
+      uint32_t s[64];
       __syncwarp();
-      {
+      if (mine) {
         uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
         uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-        tmem_ld32(tmem + lane_off + b * 128, s0);
-        tmem_ld32(tmem + lane_off + b * 128 + 32, s1);
-        if (has1) {
-          uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
-          uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
-          tmem_ld32(tmem + lane_off + b * 128 + 64, s2);
-          tmem_ld32(tmem + lane_off + b * 128 + 96, s3);
-        }
+        tmem_ld32(tmem + lane_off + b * 128 + half * 64, s0);
+        tmem_ld32(tmem + lane_off + b * 128 + half * 64 + 32, s1);
         tmem_wait_ld();
       }
       tc_fence_before();
       mbar_arrive(&s_free[b]);
 
-      const int n0 = (int)min((int64_t)64, a.Lk - (int64_t)j0 * 64);
-      const int n1 = has1 ? (int)min((int64_t)64, a.Lk - (int64_t)j1 * 64) : 0;
-      const bool full = n0 == 64 && (!has1 || n1 == 64);
-      const float c0 = qs * __ldg(a.k_scale + (int64_t)h * a.Kb + j0) * a.scale_log2;
-      const float c1 = has1 ? qs * __ldg(a.k_scale + (int64_t)h * a.Kb + j1) * a.scale_log2 : 0.f;
-      // tile max on the raw int32 scores (scales are positive)
-      int mx0 = INT_MIN, mx1 = INT_MIN;
-      if (full) {
+      const int n = mine ? (int)min((int64_t)64, a.Lk - (int64_t)jb * 64) : 0;
+      const float c = mine ? qs * __ldg(a.k_scale + (int64_t)h * a.Kb + jb) * a.scale_log2 : 0.f;
+      // tile max of this half on the raw int32 scores (scales are positive)
+      int mx = INT_MIN;
+      if (n == 64) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) mx0 = max(mx0, (int)s[c]);
-        if (has1) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) mx1 = max(mx1, (int)s[64 + c]);
-        }
+        for (int cc = 0; cc < 64; ++cc) mx = max(mx, (int)s[cc]);
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c < n0) mx0 = max(mx0, (int)s[c]);
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c < n1) mx1 = max(mx1, (int)s[64 + c]);
+        for (int cc = 0; cc < 64; ++cc)
+          if (cc < n) mx = max(mx, (int)s[cc]);
       }
-      float tmax = (float)mx0 * c0;
-      if (n1 > 0) tmax = fmaxf(tmax, (float)mx1 * c1);
+      const float ninf = -__int_as_float(0x7f800000);
+      const float hmax = n > 0 ? (float)mx * c : ninf;
+      // exchange the half-row maxima with the partner warp of this quadrant
+      // (double-buffered slot; bounded mbarrier wait instead of a named barrier)
+      xchg[((i & 1) * 2 + half) * 128 + r] = hmax;
+      mbar_arrive(&xbar[quad]);
+      if (!mbar_wait_warp(&xbar[quad], (uint32_t)(i & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      const float tmax = fmaxf(hmax, xchg[((i & 1) * 2 + (half ^ 1)) * 128 + r]);
       // lazy running max: move it only when this tile exceeds it by more than kTau
       const bool move = tmax > m + kTau;
       const float m_new = move ? tmax : m;
@@ -307,22 +312,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool rescale = __any_sync(0xffffffffu, move && i > 0);
       const float alpha = ex2(m - m_new);
       // x = S*c + log2(112) - m, with float(S) = as_float(S + 0x4B400000) - 12582912
-      const float off = kLog2_112 - m_new;
-      const float o0 = off - 12582912.0f * c0, o1 = off - 12582912.0f * c1;
-      const int ncols = has1 ? 128 : 64;
+      const float oo = kLog2_112 - m_new - 12582912.0f * c;
+      if (mine) {
 #pragma unroll
-      for (int c = 0; c < 128; c += 2) {
-        if (c < ncols) {
-          const float cc = c < 64 ? c0 : c1, oo = c < 64 ? o0 : o1;
-          const float x0 = fmaf(__int_as_float((int)s[c] + 0x4B400000), cc, oo);
-          const float x1 = fmaf(__int_as_float((int)s[c + 1] + 0x4B400000), cc, oo);
+        for (int cc = 0; cc < 64; cc += 2) {
+          const float x0 = fmaf(__int_as_float((int)s[cc] + 0x4B400000), c, oo);
+          const float x1 = fmaf(__int_as_float((int)s[cc + 1] + 0x4B400000), c, oo);
           uint32_t e = ex2_f16x2(pack_f16x2(x0, x1));
-          if (!full) {
-            const int lim = c < 64 ? n0 : n1, cl = c & 63;
-            if (cl >= lim) e &= 0xffff0000u;   // low half: column c (f16 +0 after masking)
-            if (cl + 1 >= lim) e &= 0x0000ffffu;
+          if (n < 64) {
+            if (cc >= n) e &= 0xffff0000u;      // low half: column cc -> +0
+            if (cc + 1 >= n) e &= 0x0000ffffu;
           }
-          s[c >> 1] = e;   // packed f16 pair, reuses the first half of s[]
+          s[cc >> 1] = e;   // packed f16 pair, reuses the first half of s[]
         }
       }
 
@@ -335,13 +336,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         __syncwarp();
 #pragma unroll 1
-        for (int c = 0; c < kON; c += 16) {
+        for (int cc = o_c0; cc < o_c1; cc += 16) {
           uint32_t o[16];
-          tmem_ld16(o_addr + c, o);
+          tmem_ld16(o_addr + cc, o);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st16(o_addr + c, o);
+          tmem_st16(o_addr + cc, o);
         }
         tmem_wait_st();
       }
@@ -351,16 +352,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = false;
         break;
       }
-      // P row -> shared memory, K-major, 128-byte swizzle (chunk c at c ^ (r & 7))
-      uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
+      if (mine) {
+        // this half of the P row -> shared memory, K-major, 128-byte swizzle
+        // (16-byte chunk c of the row lives at chunk c ^ (r & 7))
+        uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        if (c < (ncols >> 4)) {
+        for (int cq = 0; cq < 4; ++cq) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            w[e] = f16x2_to_e4m3x2(s[8 * c + 2 * e]) | (f16x2_to_e4m3x2(s[8 * c + 2 * e + 1]) << 16);
-          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            w[e] = f16x2_to_e4m3x2(s[8 * cq + 2 * e]) | (f16x2_to_e4m3x2(s[8 * cq + 2 * e + 1]) << 16);
+          const int chunk = half * 4 + cq;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       fence_proxy_async_smem();
@@ -369,8 +372,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       m = m_new;
       ++i;
     }
-    // epilogue: O / l * v_scale, l from the ones columns
-    uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128;
+    // epilogue: this warp's 64 output channels, O / l * v_scale, l from the ones columns
+    uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128 + half * 64;
     if (ok && i >= 1) {
       if (mbar_wait_warp(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
                          H3B_STATUS_ATTN_TIMEOUT)) {
@@ -382,25 +385,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float l = __uint_as_float(lsum[0]);
         const float inv_l = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 16) {
+        for (int cc = 0; cc < 64; cc += 16) {
           uint32_t o[16];
-          tmem_ld16(o_addr + c, o);
+          tmem_ld16(o_addr + half * 64 + cc, o);
           tmem_wait_ld();
           uint32_t packed[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float v0 = __uint_as_float(o[2 * e]) * inv_l * __ldg(a.v_scale + h * 128 + c + 2 * e);
-            const float v1 = __uint_as_float(o[2 * e + 1]) * inv_l * __ldg(a.v_scale + h * 128 + c + 2 * e + 1);
+            const int d = half * 64 + cc + 2 * e;
+            const float v0 = __uint_as_float(o[2 * e]) * inv_l * __ldg(a.v_scale + h * 128 + d);
+            const float v1 = __uint_as_float(o[2 * e + 1]) * inv_l * __ldg(a.v_scale + h * 128 + d + 1);
             packed[e] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
           }
           if (row_ok) {
-            *reinterpret_cast<uint4*>(dst + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            *reinterpret_cast<uint4*>(dst + c + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            *reinterpret_cast<uint4*>(dst + cc) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            *reinterpret_cast<uint4*>(dst + cc + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
           }
         }
       }
     } else if (row_ok && i == 0) {
-      for (int c = 0; c < 128; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
+      for (int cc = 0; cc < 64; cc += 8) *reinterpret_cast<uint4*>(dst + cc) = make_uint4(0, 0, 0, 0);
     }
   }
 
