@@ -1,82 +1,134 @@
 // attn.cu -- SageAttention-style quantized attention for sm_100a, dense or
 // driven by a Sparge block bitmap.
 //
-//   S = Q_i8 . K_i8^T   tcgen05.mma kind::i8, int32 in tensor memory
+//   S = Q_i8 . K_i8^T   tcgen05.mma kind::i8 into tensor memory that was
+//       pre-filled with 0x4B400000: the accumulator then holds the bits of the
+//       float 1.5*2^23 + S (|S| < 2^22), so S needs no integer->float conversion
+//       and the block maximum is an integer maximum of the raw bits
 //   P = exp2(S * qs * ks * scale * log2 e - m) * 112 -> E4M3 (shared memory);
-//       exp2 runs on packed f16 pairs (ex2.approx.f16x2: two exponentials per
-//       MUFU op; f16 is far finer than the E4M3 result), m is a lazily updated
-//       running max: it moves only when a tile's max exceeds it by more than
-//       kTau = 2, so P <= 2^kTau * 112 = 448 (the E4M3 maximum) and the O
-//       rescale in tensor memory is rare
-//   [O | l] += P . [V | 1]   tcgen05.mma kind::f8f6f4, N = 144: the 16 extra
-//       columns of ones give the row sum of exactly the E4M3 P that meets V
-//   out = O / l * v_scale[d] -> bf16
+//       m is a lazily updated running max: it moves (to the tile max) only when
+//       a tile's scores exceed it by more than kTau = 2, so P <= 2^kTau * 112 =
+//       448, the E4M3 maximum, and the O rescale in tensor memory is rare.
+//       Three columns in four take ex2.approx (MUFU), the fourth a polynomial
+//       on the FMA pipe (packed fp32 pairs), which balances the two pipes.
+//   O += P . V          tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32, tensor memory)
+//   out = O / l * v_scale[d] -> bf16, l the fp32 row sum of P
 //
-// One CTA per (128-query tile, head), 320 threads:
-//   warp 0      TMA producer: the Q tile once, then K/V for each PAIR of selected
-//               64-key blocks (K: 2 x [64 x 128 B], 128-byte swizzle; V^T: 2 x
-//               [128 x 64 B], 64-byte swizzle) into a 3-stage ring; no multicast
-//   warp 1      TMEM allocator + MMA issuer: S for pair i into one of two S
-//               buffers, then O += P(i-1) . V(i-1) once the softmax published P(i-1)
-//   warps 2..9  softmax, two warps per TMEM lane quadrant: for its 32 query rows
-//               warp 2..5 takes key columns 0..63 (block j0), warp 6..9 columns
-//               64..127 (block j1); the two exchange only their tile max per row
-//               through shared memory (named barrier per quadrant), then each
-//               writes its half of the P row (128-byte-swizzled K-major, as the
-//               MMA reads it), rescales its half of the O row in TMEM when the
-//               running max moves, and normalises its half of the output.
-// TMEM: S0 cols 0..127, S1 128..255, [O | l] 256..399.  Blocks are visited in
-// ascending order; a trailing unpaired block uses N = 64 / K = 64 MMAs.
+// One CTA per (two 128-query tiles A and B, head), 384 threads:
+//   warp 0      TMA producer: both Q tiles once, then one step per PAIR of
+//               selected 64-key blocks (K: 2 x [64 x 128 B], 128-byte swizzle;
+//               V^T: 2 x [128 x 64 B], 64-byte swizzle) into a 4-stage ring; no
+//               multicast.  The steps interleave the two tiles' own block
+//               lists (A, B, A, B, ...); a step whose pair both tiles selected
+//               next (every step of dense attention) serves both tiles
+//   warp 1      TMEM allocator + MMA issuer, ping-pong between the tiles:
+//               S_A(k), PV_A(previous A step), S_B(k'), PV_B(previous B step)
+//   warps 2, 3  idle (they complete the first warpgroup)
+//   warps 4..7  softmax of tile A, warps 8..11 of tile B: one query row per
+//               thread (its TMEM lane): S row from TMEM, per-block dequant
+//               scales, online max / sum, P row to shared memory in the
+//               128-byte-swizzled K-major layout the MMA reads, the S columns
+//               re-biased, O rescaled when the max moves, final normalisation.
+// Every SM sub-partition thus runs two independent softmax warps (one per
+// tile), and in dense attention each K/V pair is loaded once for 256 queries.
+// TMEM: S_A 0..127, S_B 128..255, O_A 256..383, O_B 384..511.
 #include "h3b_kernels.cuh"
 
 namespace h3b {
 
-constexpr int kAttnThreads = 320;
-constexpr int kSoftmaxThreads = 256;
-constexpr int kKVStages = 3;
+constexpr int kAttnThreads = 384;  // three warpgroups
+// Register split (setmaxnreg): the launch gives every thread kLaunchRegs (the
+// __launch_bounds__ cap for 384 threads); the producer / MMA warpgroup drops to
+// kCtrlRegs and each softmax warpgroup rises to kSoftmaxRegs.  The split must
+// not exceed the launch total, or the increase would wait forever; the host
+// checks the compiled register count against kLaunchRegs before launching.
+constexpr int kLaunchRegs = 168;
+constexpr int kCtrlRegs = 64;
+constexpr int kSoftmaxRegs = 216;
+static_assert(128 * (kCtrlRegs + 2 * kSoftmaxRegs) <= kAttnThreads * kLaunchRegs, "register split too large");
+constexpr int kTileThreads = 128;
+constexpr int kKVStages = 4;
 constexpr int kQBytes = 128 * 128;
 constexpr int kPBytes = 128 * 128;
-// K pair 16 KB, then per V block an [128 x 64 B] tile followed by a 1 KB block
-// of E4M3 ones (16 rows): the P.V MMA reads 144 rows = V^T plus the ones.
-constexpr int kVTile = 8192 + 1024;
-constexpr int kKVBytes = 16384 + 2 * kVTile;
-constexpr int kOffQ = 0;
-constexpr int kOffP = kOffQ + kQBytes;            // 2 buffers
+constexpr int kKVBytes = 32768;  // K pair 16 KB + V^T pair 2 x 8 KB
+constexpr int kOffQ = 0;                          // 2 tiles
+constexpr int kOffP = kOffQ + 2 * kQBytes;        // 2 tiles
 constexpr int kOffKV = kOffP + 2 * kPBytes;
 constexpr int kOffBar = kOffKV + kKVStages * kKVBytes;
-constexpr int kOffXchg = kOffBar + 256;            // float [2 parity][2 halves][128 rows]
-constexpr int kAttnSmem = kOffXchg + 2 * 2 * 128 * 4 + 1024;
+constexpr int kAttnSmem = kOffBar + 256 + 1024;
 constexpr float kLog2_112 = 6.807354922057604f;
 constexpr float kTau = 2.0f;
-constexpr int kON = 144;  // O columns incl. the row-sum block
+constexpr uint32_t kMagic = 0x4B400000u;          // bits of 12582912.0f = 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;
 
-
-// Ascending walk over the K blocks of one query tile.
-struct BlockIter {
+// One query tile's selected K blocks, ascending, taken two at a time.
+struct TileStream {
   const uint32_t* row;
   int words, w, Kb, dense_next;
-  uint32_t bits;
-  __device__ void init(const AttnArgs& a, int h, int qt) {
-    Kb = a.Kb;
+  bool dense;
+  uint32_t u;
+  __device__ void init(const AttnArgs& a, int h, int qt, bool active) {
+    Kb = active ? a.Kb : 0;
     dense_next = 0;
-    if (a.bitmap) {
-      row = a.bitmap + ((int64_t)h * ((a.Lq + 127) / 128) + qt) * a.words;
+    dense = a.bitmap == nullptr || !active;
+    u = 0;
+    w = 0;
+    words = 0;
+    if (!dense) {
+      const int64_t qb = (a.Lq + 127) / 128;
+      row = a.bitmap + ((int64_t)h * qb + qt) * a.words;
       words = a.words;
-      w = 0;
-      bits = words > 0 ? row[0] : 0u;
-    } else {
-      row = nullptr;
+      u = words > 0 ? row[0] : 0u;
     }
   }
-  __device__ int next() {
-    if (!row) return dense_next < Kb ? dense_next++ : -1;
-    while (bits == 0) {
+  __device__ int next_block() {
+    if (dense) return dense_next < Kb ? dense_next++ : -1;
+    while (u == 0) {
       if (++w >= words) return -1;
-      bits = row[w];
+      u = row[w];
     }
-    const int b = __ffs(bits) - 1;
-    bits &= bits - 1;
+    const int b = __ffs(u) - 1;
+    u &= u - 1;
     return w * 32 + b;
+  }
+  // blocks j0 < j1 (j1 = -1 when the tile selected an odd number of blocks)
+  __device__ bool next_pair(int& j0, int& j1) {
+    j0 = next_block();
+    if (j0 < 0) return false;
+    j1 = next_block();
+    return true;
+  }
+};
+
+// The K/V load schedule of a CTA: the two tiles' pair streams interleaved
+// (A, B, A, B, ...); when both tiles' next pairs are the same blocks (always so
+// for dense attention) one step serves both.  who: bit 0 tile A, bit 1 tile B.
+struct StepIter {
+  TileStream ta, tb;
+  int a0, a1, b0, b1;
+  bool pa, pb, turn_b;
+  __device__ void init(const AttnArgs& a, int h, int qta, bool has_b) {
+    ta.init(a, h, qta, true);
+    tb.init(a, h, qta + 1, has_b);
+    pa = ta.next_pair(a0, a1);
+    pb = tb.next_pair(b0, b1);
+    turn_b = false;
+  }
+  __device__ bool pending(int t) const { return t ? pb : pa; }
+  __device__ bool next(int& j0, int& j1, int& who) {
+    if (!pa && !pb) return false;
+    if (pa && pb && a0 == b0 && a1 == b1)
+      who = 3;
+    else if (pa && (!pb || !turn_b))
+      who = 1;
+    else
+      who = 2;
+    j0 = who == 2 ? b0 : a0;
+    j1 = who == 2 ? b1 : a1;
+    if (who & 1) pa = ta.next_pair(a0, a1);
+    if (who & 2) pb = tb.next_pair(b0, b1);
+    if (who != 3) turn_b = who == 1;
+    return true;
   }
 };
 
@@ -85,25 +137,207 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// two floats -> packed f16 pair (lo in bits 0..15), round to nearest
-__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-// packed f16 pair -> two E4M3 bytes (satfinite, round to nearest even), lo byte = lo half
-__device__ __forceinline__ uint32_t f16x2_to_e4m3x2(uint32_t x) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(x));
-  return (uint32_t)r;
-}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- softmax pieces
+// All loops are fully unrolled over compile-time column ranges (NC = 64: one
+// key block, 128: a pair), so the per-column work has no branches and the
+// compiler can interleave the independent columns.
+#define H3B_S32(arr, off) (*reinterpret_cast<uint32_t(*)[32]>(&(arr)[off]))
+
+// 2^f on [-0.5, 0.5]: degree-3 polynomial fitted for this kernel (weighted least
+// squares on Chebyshev nodes, relative error < 7.5e-5)
+constexpr float kP0 = 0.9999280571937561f, kP1 = 0.6932609677314758f, kP2 = 0.2426111251115799f,
+                kP3 = 0.05517164617776871f;
+// 2^x on the FMA pipe: j = rint(x) by the 1.5 * 2^23 rounding constant (whose
+// low bits then hold j), 2^(x - j) by the polynomial, j added to the exponent
+// field.  x is clamped at -125, so the result stays a normal float (< 2^-124).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + kMagicF;
+  const float f = x - (t - kMagicF);
+  const float p = fmaf(fmaf(fmaf(kP3, f, kP2), f, kP1), f, kP0);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+// four floats -> four E4M3 bytes (satfinite, round to nearest even), a lowest
+__device__ __forceinline__ uint32_t e4m3x4_f32(float a, float b, float c, float d) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n\t"
+      "mov.b32 %0, {lo, hi};\n\t}"
+      : "=r"(r) : "f"(a), "f"(b), "f"(c), "f"(d));
+  return r;
+}
+// maximum of the 64 raw columns [CB, CB + 64); the biased accumulator bits are
+// positive floats, so integer order is score order
+template <int CB>
+__device__ __forceinline__ int raw_max64(const uint32_t (&s)[128]) {
+  int m0 = (int)s[CB], m1 = (int)s[CB + 1], m2 = (int)s[CB + 2], m3 = (int)s[CB + 3];
+#pragma unroll
+  for (int c = 4; c < 64; c += 4) {
+    m0 = max(m0, (int)s[CB + c]);
+    m1 = max(m1, (int)s[CB + c + 1]);
+    m2 = max(m2, (int)s[CB + c + 2]);
+    m3 = max(m3, (int)s[CB + c + 3]);
+  }
+  return max(max(m0, m1), max(m2, m3));
+}
+// the same over the first n (1..63) columns of a ragged last block; the other
+// columns become -inf, which the exponential maps to 0
+template <int CB>
+__device__ __forceinline__ int raw_max_ragged(uint32_t (&s)[128], int n) {
+  int m0 = (int)s[CB];
+#pragma unroll
+  for (int c = 1; c < 64; ++c) {
+    if (c < n)
+      m0 = max(m0, (int)s[CB + c]);
+    else
+      s[CB + c] = 0xff800000u;
+  }
+  return m0;
+}
+// P = 2^(S * cc + oo) over columns [CB, CB + 64), written back as floats, on
+// packed fp32 pairs (FFMA2 / FADD2).  Of every 8 columns, 6 take ex2.approx
+// (MUFU) and 2 the polynomial exponential on the FMA pipe; returns the sum.
+template <int CB>
+__device__ __forceinline__ float exp_block(uint32_t (&s)[128], float cc, float oo) {
+  const float2 c2 = make_float2(cc, cc), o2 = make_float2(oo, oo);
+  const float2 kM = make_float2(kMagicF, kMagicF), kNM = make_float2(-kMagicF, -kMagicF);
+  const float2 kN1 = make_float2(-1.f, -1.f);
+  const float2 q0 = make_float2(kP0, kP0), q1 = make_float2(kP1, kP1), q2 = make_float2(kP2, kP2),
+               q3 = make_float2(kP3, kP3);
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < 64; c += 8) {
+    float2 x[4], p[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      x[k] = __ffma2_rn(make_float2(__uint_as_float(s[CB + c + 2 * k]), __uint_as_float(s[CB + c + 2 * k + 1])),
+                        c2, o2);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) p[k] = make_float2(ex2(x[k].x), ex2(x[k].y));
+    {
+      // 2^x = 2^j * 2^f, j = rint(x) (low bits of t), f = x - j (exact)
+      const float2 xp = make_float2(fmaxf(x[3].x, -125.0f), fmaxf(x[3].y, -125.0f));
+      const float2 t = __fadd2_rn(xp, kM);
+      const float2 f = __ffma2_rn(__fadd2_rn(t, kNM), kN1, xp);
+      const float2 q = __ffma2_rn(__ffma2_rn(__ffma2_rn(q3, f, q2), f, q1), f, q0);
+      p[3] = make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                         __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+    }
+    acc0 = __fadd2_rn(acc0, p[0]);
+    acc1 = __fadd2_rn(acc1, p[1]);
+    acc0 = __fadd2_rn(acc0, p[2]);
+    acc1 = __fadd2_rn(acc1, p[3]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s[CB + c + 2 * k] = __float_as_uint(p[k].x);
+      s[CB + c + 2 * k + 1] = __float_as_uint(p[k].y);
+    }
+  }
+  const float2 t = __fadd2_rn(acc0, acc1);
+  return t.x + t.y;
+}
+// P row -> shared memory, K-major, 128-byte swizzle (16-byte chunk c at c ^ (r & 7))
+template <int NC>
+__device__ __forceinline__ void store_p(const uint32_t (&s)[128], uint8_t* prow, int r) {
+#pragma unroll
+  for (int c = 0; c < NC / 16; ++c) {
+    const uint4 w = make_uint4(e4m3x4_f32(__uint_as_float(s[16 * c]), __uint_as_float(s[16 * c + 1]),
+                                          __uint_as_float(s[16 * c + 2]), __uint_as_float(s[16 * c + 3])),
+                               e4m3x4_f32(__uint_as_float(s[16 * c + 4]), __uint_as_float(s[16 * c + 5]),
+                                          __uint_as_float(s[16 * c + 6]), __uint_as_float(s[16 * c + 7])),
+                               e4m3x4_f32(__uint_as_float(s[16 * c + 8]), __uint_as_float(s[16 * c + 9]),
+                                          __uint_as_float(s[16 * c + 10]), __uint_as_float(s[16 * c + 11])),
+                               e4m3x4_f32(__uint_as_float(s[16 * c + 12]), __uint_as_float(s[16 * c + 13]),
+                                          __uint_as_float(s[16 * c + 14]), __uint_as_float(s[16 * c + 15])));
+    *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = w;
+  }
+}
+template <int NC>
+__device__ __forceinline__ void rebias_s(uint32_t s_addr) {
+  __syncwarp();
+  tmem_st32_const(s_addr, kMagic);
+  tmem_st32_const(s_addr + 32, kMagic);
+  if constexpr (NC == 128) {
+    tmem_st32_const(s_addr + 64, kMagic);
+    tmem_st32_const(s_addr + 96, kMagic);
+  }
+}
+
+// One key pair (or a single trailing block, NC = 64) for one query row of one
+// tile.  The second block's scores load from TMEM while the first block's
+// maximum is taken.  The running max m moves (to the tile max) only when the
+// tile max exceeds it by more than kTau; then O is rescaled.  cnt = steps this
+// tile already processed: the PV of step cnt - 1 may still be running and is
+// waited for, on pv_done, only before O is rescaled or P is overwritten.
+template <int NC>
+__device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint8_t* prow, int r, float c0,
+                                             float c1, int n0, int n1, int cnt, float& m, float& l,
+                                             uint64_t* pv_done, volatile int* abort_flag) {
+  uint32_t s[128];
+  __syncwarp();
+  tmem_ld32(s_addr, H3B_S32(s, 0));
+  tmem_ld32(s_addr + 32, H3B_S32(s, 32));
+  tmem_wait_ld_dep(H3B_S32(s, 0));
+  reg_barrier32(H3B_S32(s, 32));
+  if constexpr (NC == 128) {
+    tmem_ld32(s_addr + 64, H3B_S32(s, 64));
+    tmem_ld32(s_addr + 96, H3B_S32(s, 96));
+  }
+  const int mx0 = n0 == 64 ? raw_max64<0>(s) : raw_max_ragged<0>(s, n0);
+  float tmax = (__int_as_float(mx0) - kMagicF) * c0;
+  if constexpr (NC == 128) {
+    tmem_wait_ld_dep(H3B_S32(s, 64));
+    reg_barrier32(H3B_S32(s, 96));
+    const int mx1 = n1 == 64 ? raw_max64<64>(s) : raw_max_ragged<64>(s, n1);
+    tmax = fmaxf(tmax, (__int_as_float(mx1) - kMagicF) * c1);
+  }
+  const float m_new = tmax > m + kTau ? tmax : m;
+  float alpha = 1.f;
+  bool pv_waited = false;
+  if (__any_sync(0xffffffffu, m_new != m)) {
+    alpha = ex2(m - m_new);
+    m = m_new;
+    if (cnt > 0) {
+      if (!mbar_wait_warp(pv_done, (uint32_t)((cnt - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
+      pv_waited = true;
+      tc_fence_after();
+      __syncwarp();
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 16) {
+        uint32_t o[16];
+        tmem_ld16(o_addr + c, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+        tmem_st16(o_addr + c, o);
+      }
+    }
+  }
+  rebias_s<NC>(s_addr);
+  const float off = kLog2_112 - m;
+  float psum = exp_block<0>(s, c0, off - kMagicF * c0);
+  if constexpr (NC == 128) psum += exp_block<64>(s, c1, off - kMagicF * c1);
+  if (cnt > 0 && !pv_waited) {
+    if (!mbar_wait_warp(pv_done, (uint32_t)((cnt - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
+  }
+  store_p<NC>(s, prow, r);
+  tmem_wait_st();
+  fence_proxy_async_smem();
+  tc_fence_before();
+  l = l * alpha + psum;
+  return true;
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -112,19 +346,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;                  // 1
-  uint64_t* kv_full = bars + 1;             // kKVStages
-  uint64_t* kv_empty = kv_full + kKVStages; // kKVStages
-  uint64_t* s_full = kv_empty + kKVStages;  // 2
-  uint64_t* s_free = s_full + 2;            // 2
-  uint64_t* p_full = s_free + 2;            // 2
-  uint64_t* pv_done = p_full + 2;           // 2 (one per P buffer)
-  uint64_t* xbar = pv_done + 2;             // 4: tile-max exchange per lane quadrant (64 threads)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
+  uint64_t* q_full = bars;                   // 1
+  uint64_t* kv_full = bars + 1;              // kKVStages
+  uint64_t* kv_empty = kv_full + kKVStages;  // kKVStages
+  uint64_t* s_full = kv_empty + kKVStages;   // 2 (per tile): S MMA done
+  uint64_t* pv_done = s_full + 2;            // 2 (per tile): PV MMA done
+  uint64_t* p_full = pv_done + 2;            // 2 (per tile, 128 arrivals): P written, S read
+  uint64_t* o_full = p_full + 2;             // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y;
+  const int h = blockIdx.y;
+  const int qta = 2 * blockIdx.x;
+  const int num_qt = (int)((a.Lq + 127) / 128);
+  const bool has_b = qta + 1 < num_qt;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -132,24 +368,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], kSoftmaxThreads);
-      mbar_init(&p_full[b], kSoftmaxThreads);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&p_full[t], kTileThreads);
     }
-    mbar_init(&pv_done[0], 1);
-    mbar_init(&pv_done[1], 1);
-    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 64);
+    mbar_init(o_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  // constant E4M3 ones after every V tile (never overwritten by TMA)
-  for (int i = threadIdx.x; i < kKVStages * 2 * 64; i += blockDim.x) {
-    const int st = i / 128, blk = (i / 64) & 1, w = i & 63;
-    reinterpret_cast<uint4*>(smem + kOffKV + st * kKVBytes + 16384 + blk * kVTile + 8192)[w] =
-        make_uint4(0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u);
-  }
-  fence_proxy_async_smem();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -163,20 +390,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp >= 4) {
+    // bias both S accumulators: every S MMA accumulates onto 1.5 * 2^23
+    const int t = (warp - 4) >> 2;
+    const uint32_t sa = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(t * 128);
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) tmem_st32_const(sa + c, kMagic);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
-  BlockIter it;
-  it.init(a, h, qt);
-
+  if (warp < 4) {
+    // each register change sits inside its role's branch, so the compiler
+    // budgets every role's code by that role's own limit
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
+  }
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      tma_load_2d(smem + kOffQ, &tmQ, q_full, 0, (int)(h * a.Lqpad + (int64_t)qt * 128));
+      StepIter it;
+      it.init(a, h, qta, has_b);
+      mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+      tma_load_2d(smem + kOffQ, &tmQ, q_full, 0, (int)(h * a.Lqpad + (int64_t)qta * 128));
+      tma_load_2d(smem + kOffQ + kQBytes, &tmQ, q_full, 0, (int)(h * a.Lqpad + (int64_t)(qta + 1) * 128));
       int stage = 0;
       uint32_t phase = 0;
-      while (true) {
-        const int j0 = it.next();
-        if (j0 < 0) break;
-        const int j1 = it.next();
+      int j0, j1, who;
+      while (it.next(j0, j1, who)) {
         if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) break;
         uint8_t* kst = smem + kOffKV + stage * kKVBytes;
         uint8_t* vst = kst + 16384;
@@ -185,226 +427,158 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_2d(vst, &tmV, &kv_full[stage], j0 * 64, h * 128);
         if (j1 >= 0) {
           tma_load_2d(kst + 8192, &tmK, &kv_full[stage], 0, (int)(h * a.Lkpad + (int64_t)j1 * 64));
-          tma_load_2d(vst + kVTile, &tmV, &kv_full[stage], j1 * 64, h * 128);
+          tma_load_2d(vst + 8192, &tmV, &kv_full[stage], j1 * 64, h * 128);
         }
         if (++stage == kKVStages) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // per step, for each tile it serves: [wait P of the tile's previous step]
+      // S(this step), PV(previous step); a stage is released once every tile it
+      // served has issued its PV on it
+      StepIter it;
+      it.init(a, h, qta, has_b);
       bool ok = mbar_wait(q_full, 0, abort_flag, H3B_STATUS_ATTN_TIMEOUT);
-      const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ));
-      int stage = 0, prev_stage = 0, i = 0;
+      constexpr uint32_t idesc_pv = idesc_e4m3(128, 128);
+      int stage = 0;
       uint32_t phase = 0;
-      bool prev_has1 = false;
-      constexpr uint32_t idesc_pv = idesc_e4m3(128, kON);
-      auto issue_pv = [&](int pi) -> bool {
-        const int pb = pi & 1;
-        if (!mbar_wait(&p_full[pb], (uint32_t)((pi >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
+      int pst[2] = {-1, -1};
+      bool ptwo[2] = {false, false};
+      bool first_pv[2] = {true, true};
+      int p_cnt[2] = {0, 0};
+      uint32_t rem = 0;  // per stage (4 bits each): tiles that still have to issue a PV on it
+      auto wait_p = [&](int t) -> bool {
+        if (!mbar_wait(&p_full[t], (uint32_t)(p_cnt[t] & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
+        ++p_cnt[t];
         tc_fence_after();
-        const uint32_t pbase = smem_u32(smem + kOffP + pb * kPBytes);
-        const uint32_t vbase = smem_u32(smem + kOffKV + prev_stage * kKVBytes + 16384);
-        const int ksteps = prev_has1 ? 4 : 2;
-        for (int k = 0; k < ksteps; ++k) {
-          const uint64_t pd = sdesc_kmajor_sw128(pbase + 32 * k);
-          const uint64_t vd = sdesc_kmajor_sw64(vbase + (k >> 1) * kVTile + (k & 1) * 32);
-          mma_f8_ss(tmem + 256, pd, vd, idesc_pv, (pi > 0 || k > 0) ? 1u : 0u);
-        }
-        mma_commit(&pv_done[pb]);
-        mma_commit(&kv_empty[prev_stage]);
         return true;
       };
-      while (ok) {
-        const int j0 = it.next();
-        if (j0 < 0) break;
-        const int j1 = it.next();
-        const bool has1 = j1 >= 0;
-        const int b = i & 1;
+      auto issue_pv = [&](int t) {
+        const uint32_t pbase = smem_u32(smem + kOffP + t * kPBytes);
+        const uint32_t vbase = smem_u32(smem + kOffKV + pst[t] * kKVBytes + 16384);
+        const uint32_t d = tmem + 256 + (uint32_t)(t * 128);
+        const int ks = ptwo[t] ? 4 : 2;
+        for (int k = 0; k < ks; ++k)
+          mma_f8_ss(d, sdesc_kmajor_sw128(pbase + 32 * k), sdesc_kmajor_sw64(vbase + (k >> 1) * 8192 + (k & 1) * 32),
+                    idesc_pv, (!first_pv[t] || k > 0) ? 1u : 0u);
+        mma_commit(&pv_done[t]);
+        first_pv[t] = false;
+        rem -= 1u << (4 * pst[t]);
+        if (((rem >> (4 * pst[t])) & 0xfu) == 0) mma_commit(&kv_empty[pst[t]]);
+        pst[t] = -1;
+      };
+      int j0, j1, who;
+      while (ok && it.next(j0, j1, who)) {
         if (!mbar_wait(&kv_full[stage], phase, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
-        if (!mbar_wait(&s_free[b], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
-          ok = false;
-          break;
-        }
         tc_fence_after();
         const uint32_t kbase = smem_u32(smem + kOffKV + stage * kKVBytes);
-        const uint32_t idesc_s = has1 ? idesc_i8(128, 128) : idesc_i8(128, 64);
+        const bool two = j1 >= 0;
+        rem |= (uint32_t)((who & 1) + (who >> 1)) << (4 * stage);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_i8_ss(tmem + (uint32_t)(b * 128), qdesc + (uint64_t)(2 * k),
-                    sdesc_kmajor_sw128(kbase + 32 * k), idesc_s, k > 0 ? 1u : 0u);
-        mma_commit(&s_full[b]);
-        if (i >= 1 && !issue_pv(i - 1)) { ok = false; break; }
-        prev_stage = stage;
-        prev_has1 = has1;
+        for (int t = 0; t < 2; ++t) {
+          if (!((who >> t) & 1)) continue;
+          if (pst[t] >= 0 && !wait_p(t)) { ok = false; break; }
+          const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ + t * kQBytes));
+          const uint32_t idesc_s = two ? idesc_i8(128, 128) : idesc_i8(128, 64);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_i8_ss(tmem + (uint32_t)(t * 128), qdesc + (uint64_t)(2 * k), sdesc_kmajor_sw128(kbase + 32 * k),
+                      idesc_s, 1u);
+          mma_commit(&s_full[t]);
+          if (pst[t] >= 0) issue_pv(t);
+          pst[t] = stage;
+          ptwo[t] = two;
+        }
+        if (!ok) break;
+        // a tile with no further steps releases its last stage now
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (((who >> t) & 1) || pst[t] < 0 || it.pending(t)) continue;
+          if (!wait_p(t)) { ok = false; break; }
+          issue_pv(t);
+        }
+        if (!ok) break;
         if (++stage == kKVStages) { stage = 0; phase ^= 1; }
-        ++i;
       }
-      if (ok && i >= 1) issue_pv(i - 1);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (!ok || pst[t] < 0) continue;
+        if (!wait_p(t)) { ok = false; break; }
+        issue_pv(t);
+      }
+      if (ok) mma_commit(o_full);
     }
-  } else {
-    // softmax warps 2..9: TMEM lane quadrant warp % 4, key-column half (warp - 2) / 4
+  } else if (warp >= 4) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // softmax: tile t, TMEM lane quadrant warp % 4, one query row per thread
+    const int t = (warp - 4) >> 2;
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
-    const int64_t qrow = (int64_t)qt * 128 + r;
+    const int64_t qrow = (int64_t)(qta + t) * 128 + r;
     const bool row_ok = qrow < a.Lq;
     const float qs = row_ok ? __ldg(a.q_scale + (int64_t)h * a.nqs + qrow / a.q_block) : 0.f;
+    const float qsl = qs * a.scale_log2;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t o_addr = tmem + lane_off + 256;
-    float* xchg = reinterpret_cast<float*>(smem + kOffXchg);   // [parity][half][row]
-    const int o_c0 = half ? 80 : 0, o_c1 = half ? kON : 80;  // this warp's O columns (16-column chunks)
-    float m = -__int_as_float(0x7f800000);
-    int i = 0;
+    const uint32_t s_addr = tmem + lane_off + (uint32_t)(t * 128);
+    const uint32_t o_addr = tmem + lane_off + 256 + (uint32_t)(t * 128);
+    uint8_t* prow = smem + kOffP + t * kPBytes + r * 128;
+    const float* ksc = a.k_scale + (int64_t)h * a.Kb;
+    TileStream ts;
+    ts.init(a, h, qta + t, t == 0 || has_b);
+    float m = -__int_as_float(0x7f800000), l = 0.f;
+    int cnt = 0;
     bool ok = true;
-    while (true) {
-      const int j0 = it.next();
-      if (j0 < 0) break;
-      const int j1 = it.next();
-      const bool has1 = j1 >= 0;
-      const int b = i & 1;
-      const int jb = half ? j1 : j0;           // this warp's key block (-1: none)
-      const bool mine = jb >= 0;
-      if (!mbar_wait_warp(&s_full[b], (uint32_t)((i >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+    int j0, j1;
+    while (ts.next_pair(j0, j1)) {
+      // the blocks' scales and valid key counts, read before the wait
+      const bool two = j1 >= 0;
+      // (a zero scale, for an all-zero query row or key block, is floored so that
+      // masked -inf columns stay -inf)
+      const float c0 = fmaxf(qsl * __ldg(ksc + j0), 1e-30f);
+      const float c1 = two ? fmaxf(qsl * __ldg(ksc + j1), 1e-30f) : 0.f;
+      const int n0 = (int)min((int64_t)64, a.Lk - (int64_t)j0 * 64);
+      const int n1 = two ? (int)min((int64_t)64, a.Lk - (int64_t)j1 * 64) : 64;
+      if (!mbar_wait_warp(&s_full[t], (uint32_t)(cnt & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s[64];
-      __syncwarp();
-      if (mine) {
-        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
-        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
-        tmem_ld32(tmem + lane_off + b * 128 + half * 64, s0);
-        tmem_ld32(tmem + lane_off + b * 128 + half * 64 + 32, s1);
-        tmem_wait_ld();
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[b]);
-
-      const int n = mine ? (int)min((int64_t)64, a.Lk - (int64_t)jb * 64) : 0;
-      const float c = mine ? qs * __ldg(a.k_scale + (int64_t)h * a.Kb + jb) * a.scale_log2 : 0.f;
-      // tile max of this half on the raw int32 scores (scales are positive)
-      int mx = INT_MIN;
-      if (n == 64) {
-#pragma unroll
-        for (int cc = 0; cc < 64; ++cc) mx = max(mx, (int)s[cc]);
-      } else {
-#pragma unroll
-        for (int cc = 0; cc < 64; ++cc)
-          if (cc < n) mx = max(mx, (int)s[cc]);
-      }
-      const float ninf = -__int_as_float(0x7f800000);
-      const float hmax = n > 0 ? (float)mx * c : ninf;
-      // exchange the half-row maxima with the partner warp of this quadrant
-      // (double-buffered slot; bounded mbarrier wait instead of a named barrier)
-      xchg[((i & 1) * 2 + half) * 128 + r] = hmax;
-      mbar_arrive(&xbar[quad]);
-      if (!mbar_wait_warp(&xbar[quad], (uint32_t)(i & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-      const float tmax = fmaxf(hmax, xchg[((i & 1) * 2 + (half ^ 1)) * 128 + r]);
-      // lazy running max: move it only when this tile exceeds it by more than kTau
-      const bool move = tmax > m + kTau;
-      const float m_new = move ? tmax : m;
-      // tcgen05.ld / st are warp-collective: rescale the whole warp's rows when any
-      // lane needs it (lanes whose max did not move scale by exactly 1)
-      const bool rescale = __any_sync(0xffffffffu, move && i > 0);
-      const float alpha = ex2(m - m_new);
-      // x = S*c + log2(112) - m, with float(S) = as_float(S + 0x4B400000) - 12582912
-      const float oo = kLog2_112 - m_new - 12582912.0f * c;
-      if (mine) {
-#pragma unroll
-        for (int cc = 0; cc < 64; cc += 2) {
-          const float x0 = fmaf(__int_as_float((int)s[cc] + 0x4B400000), c, oo);
-          const float x1 = fmaf(__int_as_float((int)s[cc + 1] + 0x4B400000), c, oo);
-          uint32_t e = ex2_f16x2(pack_f16x2(x0, x1));
-          if (n < 64) {
-            if (cc >= n) e &= 0xffff0000u;      // low half: column cc -> +0
-            if (cc + 1 >= n) e &= 0x0000ffffu;
-          }
-          s[cc >> 1] = e;   // packed f16 pair, reuses the first half of s[]
-        }
-      }
-
-      if (rescale) {
-        if (!mbar_wait_warp(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
-                            H3B_STATUS_ATTN_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        __syncwarp();
-#pragma unroll 1
-        for (int cc = o_c0; cc < o_c1; cc += 16) {
-          uint32_t o[16];
-          tmem_ld16(o_addr + cc, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st16(o_addr + cc, o);
-        }
-        tmem_wait_st();
-      }
-      // P buffer b was last read by PV(i - 2)
-      if (i >= 2 &&
-          !mbar_wait_warp(&pv_done[b], (uint32_t)(((i - 2) >> 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-      if (mine) {
-        // this half of the P row -> shared memory, K-major, 128-byte swizzle
-        // (16-byte chunk c of the row lives at chunk c ^ (r & 7))
-        uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
-#pragma unroll
-        for (int cq = 0; cq < 4; ++cq) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            w[e] = f16x2_to_e4m3x2(s[8 * cq + 2 * e]) | (f16x2_to_e4m3x2(s[8 * cq + 2 * e + 1]) << 16);
-          const int chunk = half * 4 + cq;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[b]);
-      m = m_new;
-      ++i;
+      ok = two ? softmax_step<128>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
+                                   abort_flag)
+               : softmax_step<64>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
+                                  abort_flag);
+      if (!ok) break;
+      mbar_arrive(&p_full[t]);
+      ++cnt;
     }
-    // epilogue: this warp's 64 output channels, O / l * v_scale, l from the ones columns
-    uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128 + half * 64;
-    if (ok && i >= 1) {
-      if (mbar_wait_warp(&pv_done[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), abort_flag,
-                         H3B_STATUS_ATTN_TIMEOUT)) {
+    // epilogue: O / l * v_scale
+    uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128;
+    if (ok && cnt > 0) {
+      if (mbar_wait_warp(o_full, 0u, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         tc_fence_after();
         __syncwarp();
-        uint32_t lsum[16];
-        tmem_ld16(o_addr + 128, lsum);
-        tmem_wait_ld();
-        const float l = __uint_as_float(lsum[0]);
         const float inv_l = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll 1
-        for (int cc = 0; cc < 64; cc += 16) {
+        for (int c = 0; c < 128; c += 16) {
           uint32_t o[16];
-          tmem_ld16(o_addr + half * 64 + cc, o);
+          tmem_ld16(o_addr + c, o);
           tmem_wait_ld();
           uint32_t packed[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const int d = half * 64 + cc + 2 * e;
-            const float v0 = __uint_as_float(o[2 * e]) * inv_l * __ldg(a.v_scale + h * 128 + d);
-            const float v1 = __uint_as_float(o[2 * e + 1]) * inv_l * __ldg(a.v_scale + h * 128 + d + 1);
+            const float v0 = __uint_as_float(o[2 * e]) * inv_l * __ldg(a.v_scale + h * 128 + c + 2 * e);
+            const float v1 = __uint_as_float(o[2 * e + 1]) * inv_l * __ldg(a.v_scale + h * 128 + c + 2 * e + 1);
             packed[e] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
           }
           if (row_ok) {
-            *reinterpret_cast<uint4*>(dst + cc) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            *reinterpret_cast<uint4*>(dst + cc + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            *reinterpret_cast<uint4*>(dst + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            *reinterpret_cast<uint4*>(dst + c + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
           }
         }
       }
-    } else if (row_ok && i == 0) {
-      for (int cc = 0; cc < 64; cc += 8) *reinterpret_cast<uint4*>(dst + cc) = make_uint4(0, 0, 0, 0);
+    } else if (row_ok && cnt == 0) {
+      for (int c = 0; c < 128; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
     }
   }
 
@@ -429,9 +603,15 @@ int launch_attention(const void* q, const void* k, const void* vt, const AttnArg
   if (!make_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.Lkpad, (uint64_t)(a.H * 128),
                     (uint64_t)a.Lkpad, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return 1;
-  cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, attn_kernel);
+  if (e == cudaSuccess && fa.numRegs != kLaunchRegs) {
+    *err = cudaSuccess;
+    return 3;  // the register split was planned for a different launch register count
+  }
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e == cudaSuccess) {
-    dim3 grid((unsigned)((a.Lq + 127) / 128), (unsigned)a.H);
+    dim3 grid((unsigned)(((a.Lq + 127) / 128 + 1) / 2), (unsigned)a.H);
     attn_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(tq, tk, tv, a);
     e = cudaGetLastError();
   }

@@ -295,6 +295,7 @@ int h3b_attention(const void* q, const void* q_scale, int q_block, int64_t Lq, i
   cudaError_t e = cudaSuccess;
   const int r = h3b::launch_attention(q, k, vt, a, st(stream), &e);
   if (r == 1) return fail(H3B_ERR_CUDA, "attention: cuTensorMapEncodeTiled failed");
+  if (r == 3) return fail(H3B_ERR_UNSUPPORTED, "attention: kernel register count differs from the planned split");
   return cuda_status(e, "attention");
 }
 
