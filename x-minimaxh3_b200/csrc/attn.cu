@@ -15,15 +15,18 @@
 //   out = O / l * v_scale[d] -> bf16, l the fp32 row sum of P
 //
 // One CTA per (two 128-query tiles A and B, head), 384 threads:
-//   warp 0      TMA producer: both Q tiles once, then one step per PAIR of
+//   warp 0      TMA producer (the warp runs the schedule, one elected lane
+//               issues the copies): both Q tiles once, then one step per PAIR of
 //               selected 64-key blocks (K: 2 x [64 x 128 B], 128-byte swizzle;
 //               V^T: 2 x [128 x 64 B], 64-byte swizzle) into a 4-stage ring; no
 //               multicast.  The steps interleave the two tiles' own block
 //               lists (A, B, A, B, ...); a step whose pair both tiles selected
 //               next (every step of dense attention) serves both tiles
-//   warp 1      TMEM allocator + MMA issuer, ping-pong between the tiles:
-//               S_A(k), PV_A(previous A step), S_B(k'), PV_B(previous B step)
-//   warps 2, 3  idle (they complete the first warpgroup)
+//   warp 1      TMEM allocator
+//   warps 2, 3  MMA issuers of tiles A and B (warp-wide loop over the step
+//               schedule, descriptors in uniform registers, one elected lane
+//               issues): at each of its tile's steps, once the previous P is
+//               written, S(step) and PV(previous step)
 //   warps 4..7  softmax of tile A, warps 8..11 of tile B: one query row per
 //               thread (its TMEM lane): S row from TMEM, per-block dequant
 //               scales, online max / sum, P row to shared memory in the
@@ -43,7 +46,7 @@ constexpr int kAttnThreads = 384;  // three warpgroups
 // not exceed the launch total, or the increase would wait forever; the host
 // checks the compiled register count against kLaunchRegs before launching.
 constexpr int kLaunchRegs = 168;
-constexpr int kCtrlRegs = 64;
+constexpr int kCtrlRegs = 72;
 constexpr int kSoftmaxRegs = 216;
 static_assert(128 * (kCtrlRegs + 2 * kSoftmaxRegs) <= kAttnThreads * kLaunchRegs, "register split too large");
 constexpr int kTileThreads = 128;
@@ -136,6 +139,16 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// true in exactly one lane of the (converged) warp
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -352,8 +365,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_full = kv_empty + kKVStages;   // 2 (per tile): S MMA done
   uint64_t* pv_done = s_full + 2;            // 2 (per tile): PV MMA done
   uint64_t* p_full = pv_done + 2;            // 2 (per tile, 128 arrivals): P written, S read
-  uint64_t* o_full = p_full + 2;             // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+  uint64_t* o_full = p_full + 2;             // 2 (per tile)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -366,14 +379,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(q_full, 1);
     for (int s = 0; s < kKVStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);  // one release per tile
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&pv_done[t], 1);
       mbar_init(&p_full[t], kTileThreads);
     }
-    mbar_init(o_full, 1);
+    mbar_init(&o_full[0], 1);
+    mbar_init(&o_full[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -409,17 +423,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
   }
   if (warp == 0) {
-    if (lane == 0) {
-      StepIter it;
-      it.init(a, h, qta, has_b);
+    // TMA producer: the whole warp walks the schedule (warp-uniform control
+    // flow), one elected lane issues the copies
+    StepIter it;
+    it.init(a, h, qta, has_b);
+    if (elect_one()) {
       mbar_arrive_expect_tx(q_full, 2 * kQBytes);
       tma_load_2d(smem + kOffQ, &tmQ, q_full, 0, (int)(h * a.Lqpad + (int64_t)qta * 128));
       tma_load_2d(smem + kOffQ + kQBytes, &tmQ, q_full, 0, (int)(h * a.Lqpad + (int64_t)(qta + 1) * 128));
-      int stage = 0;
-      uint32_t phase = 0;
-      int j0, j1, who;
-      while (it.next(j0, j1, who)) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) break;
+    }
+    __syncwarp();
+    int stage = 0;
+    uint32_t phase = 0;
+    int j0, j1, who;
+    while (it.next(j0, j1, who)) {
+      if (!mbar_wait_warp(&kv_empty[stage], phase ^ 1, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) break;
+      if (elect_one()) {
         uint8_t* kst = smem + kOffKV + stage * kKVBytes;
         uint8_t* vst = kst + 16384;
         mbar_arrive_expect_tx(&kv_full[stage], j1 >= 0 ? 32768u : 16384u);
@@ -429,85 +448,87 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_2d(kst + 8192, &tmK, &kv_full[stage], 0, (int)(h * a.Lkpad + (int64_t)j1 * 64));
           tma_load_2d(vst + 8192, &tmV, &kv_full[stage], j1 * 64, h * 128);
         }
-        if (++stage == kKVStages) { stage = 0; phase ^= 1; }
       }
+      __syncwarp();
+      if (++stage == kKVStages) { stage = 0; phase ^= 1; }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // per step, for each tile it serves: [wait P of the tile's previous step]
-      // S(this step), PV(previous step); a stage is released once every tile it
-      // served has issued its PV on it
-      StepIter it;
-      it.init(a, h, qta, has_b);
-      bool ok = mbar_wait(q_full, 0, abort_flag, H3B_STATUS_ATTN_TIMEOUT);
-      constexpr uint32_t idesc_pv = idesc_e4m3(128, 128);
-      int stage = 0;
-      uint32_t phase = 0;
-      int pst[2] = {-1, -1};
-      bool ptwo[2] = {false, false};
-      bool first_pv[2] = {true, true};
-      int p_cnt[2] = {0, 0};
-      uint32_t rem = 0;  // per stage (4 bits each): tiles that still have to issue a PV on it
-      auto wait_p = [&](int t) -> bool {
-        if (!mbar_wait(&p_full[t], (uint32_t)(p_cnt[t] & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
-        ++p_cnt[t];
-        tc_fence_after();
-        return true;
-      };
-      auto issue_pv = [&](int t) {
-        const uint32_t pbase = smem_u32(smem + kOffP + t * kPBytes);
-        const uint32_t vbase = smem_u32(smem + kOffKV + pst[t] * kKVBytes + 16384);
-        const uint32_t d = tmem + 256 + (uint32_t)(t * 128);
-        const int ks = ptwo[t] ? 4 : 2;
-        for (int k = 0; k < ks; ++k)
-          mma_f8_ss(d, sdesc_kmajor_sw128(pbase + 32 * k), sdesc_kmajor_sw64(vbase + (k >> 1) * 8192 + (k & 1) * 32),
-                    idesc_pv, (!first_pv[t] || k > 0) ? 1u : 0u);
+  } else if (warp == 2 || warp == 3) {
+    // MMA issuer of tile t = warp - 2: the whole warp runs the CTA's step
+    // schedule (so the descriptors live in uniform registers), one elected lane
+    // issues tcgen05.mma / commit.  At each step of its tile: [wait P of the
+    // tile's previous step] S(this step), PV(previous step).  Every stage takes
+    // one release per tile per fill (kv_empty counts 2): a commit after the
+    // tile's PV on it, or a plain arrive at the steps the tile skips.
+    const int t = warp - 2;
+    StepIter it;
+    it.init(a, h, qta, has_b);
+    bool ok = mbar_wait_warp(q_full, 0, abort_flag, H3B_STATUS_ATTN_TIMEOUT);
+    constexpr uint32_t idesc_pv = idesc_e4m3(128, 128);
+    const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ + t * kQBytes));
+    const uint32_t pbase = smem_u32(smem + kOffP + t * kPBytes);
+    const uint32_t kv_addr = smem_u32(smem + kOffKV);
+    const uint32_t s_tmem = tmem + (uint32_t)(t * 128);
+    const uint32_t o_tmem = tmem + 256 + (uint32_t)(t * 128);
+    int stage = 0;
+    uint32_t phase = 0;
+    int pst = -1;          // stage of the pending PV (-1: none)
+    bool ptwo = false, first = true;
+    uint32_t ppar = 0;     // parity of the next p_full phase
+    auto wait_p = [&]() -> bool {
+      if (!mbar_wait_warp(&p_full[t], ppar, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
+      ppar ^= 1u;
+      tc_fence_after();
+      return true;
+    };
+    auto issue_pv = [&]() {
+      const uint32_t vbase = kv_addr + (uint32_t)(pst * kKVBytes + 16384);
+      if (elect_one()) {
+        mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase), sdesc_kmajor_sw64(vbase), idesc_pv, first ? 0u : 1u);
+        mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 32), sdesc_kmajor_sw64(vbase + 32), idesc_pv, 1u);
+        if (ptwo) {
+          mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 64), sdesc_kmajor_sw64(vbase + 8192), idesc_pv, 1u);
+          mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 96), sdesc_kmajor_sw64(vbase + 8192 + 32), idesc_pv, 1u);
+        }
         mma_commit(&pv_done[t]);
-        first_pv[t] = false;
-        rem -= 1u << (4 * pst[t]);
-        if (((rem >> (4 * pst[t])) & 0xfu) == 0) mma_commit(&kv_empty[pst[t]]);
-        pst[t] = -1;
-      };
-      int j0, j1, who;
-      while (ok && it.next(j0, j1, who)) {
-        if (!mbar_wait(&kv_full[stage], phase, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t kbase = smem_u32(smem + kOffKV + stage * kKVBytes);
+        mma_commit(&kv_empty[pst]);
+      }
+      __syncwarp();
+      first = false;
+      pst = -1;
+    };
+    int j0, j1, who;
+    while (ok && it.next(j0, j1, who)) {
+      if (!mbar_wait_warp(&kv_full[stage], phase, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) { ok = false; break; }
+      tc_fence_after();
+      if ((who >> t) & 1) {
         const bool two = j1 >= 0;
-        rem |= (uint32_t)((who & 1) + (who >> 1)) << (4 * stage);
+        // S of this step reuses the S columns: the previous P must be written
+        if (pst >= 0 && !wait_p()) { ok = false; break; }
+        const uint64_t kdesc = sdesc_kmajor_sw128(kv_addr + (uint32_t)(stage * kKVBytes));
+        const uint32_t idesc_s = two ? idesc_i8(128, 128) : idesc_i8(128, 64);
+        if (elect_one()) {
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (!((who >> t) & 1)) continue;
-          if (pst[t] >= 0 && !wait_p(t)) { ok = false; break; }
-          const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ + t * kQBytes));
-          const uint32_t idesc_s = two ? idesc_i8(128, 128) : idesc_i8(128, 64);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_i8_ss(tmem + (uint32_t)(t * 128), qdesc + (uint64_t)(2 * k), sdesc_kmajor_sw128(kbase + 32 * k),
-                      idesc_s, 1u);
+          for (int k = 0; k < 4; ++k) mma_i8_ss(s_tmem, qdesc + (uint64_t)(2 * k), kdesc + (uint64_t)(2 * k), idesc_s, 1u);
           mma_commit(&s_full[t]);
-          if (pst[t] >= 0) issue_pv(t);
-          pst[t] = stage;
-          ptwo[t] = two;
         }
-        if (!ok) break;
-        // a tile with no further steps releases its last stage now
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (((who >> t) & 1) || pst[t] < 0 || it.pending(t)) continue;
-          if (!wait_p(t)) { ok = false; break; }
-          issue_pv(t);
+        __syncwarp();
+        if (pst >= 0) issue_pv();
+        pst = stage;
+        ptwo = two;
+        if (!it.pending(t)) {
+          // the tile's last step: its PV releases the stage now
+          if (!wait_p()) { ok = false; break; }
+          issue_pv();
         }
-        if (!ok) break;
-        if (++stage == kKVStages) { stage = 0; phase ^= 1; }
+      } else {
+        if (elect_one()) mbar_arrive(&kv_empty[stage]);
+        __syncwarp();
       }
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        if (!ok || pst[t] < 0) continue;
-        if (!wait_p(t)) { ok = false; break; }
-        issue_pv(t);
-      }
-      if (ok) mma_commit(o_full);
+      if (++stage == kKVStages) { stage = 0; phase ^= 1; }
+    }
+    if (ok) {
+      if (elect_one()) mma_commit(&o_full[t]);
+      __syncwarp();
     }
   } else if (warp >= 4) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
@@ -529,16 +550,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float m = -__int_as_float(0x7f800000), l = 0.f;
     int cnt = 0;
     bool ok = true;
+    // the next pair's blocks and scales are fetched one step ahead, so their
+    // latency hides behind the current step (a zero scale, for an all-zero
+    // query row or key block, is floored so that masked -inf columns stay -inf)
     int j0, j1;
-    while (ts.next_pair(j0, j1)) {
-      // the blocks' scales and valid key counts, read before the wait
+    bool have = ts.next_pair(j0, j1);
+    float c0 = 0.f, c1 = 0.f;
+    if (have) {
+      c0 = fmaxf(qsl * __ldg(ksc + j0), 1e-30f);
+      c1 = j1 >= 0 ? fmaxf(qsl * __ldg(ksc + j1), 1e-30f) : 0.f;
+    }
+    while (have) {
       const bool two = j1 >= 0;
-      // (a zero scale, for an all-zero query row or key block, is floored so that
-      // masked -inf columns stay -inf)
-      const float c0 = fmaxf(qsl * __ldg(ksc + j0), 1e-30f);
-      const float c1 = two ? fmaxf(qsl * __ldg(ksc + j1), 1e-30f) : 0.f;
       const int n0 = (int)min((int64_t)64, a.Lk - (int64_t)j0 * 64);
       const int n1 = two ? (int)min((int64_t)64, a.Lk - (int64_t)j1 * 64) : 64;
+      int nj0, nj1;
+      const bool nhave = ts.next_pair(nj0, nj1);
+      float nc0 = 0.f, nc1 = 0.f;
+      if (nhave) {
+        nc0 = __ldg(ksc + nj0);
+        nc1 = nj1 >= 0 ? __ldg(ksc + nj1) : 0.f;
+      }
       if (!mbar_wait_warp(&s_full[t], (uint32_t)(cnt & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         ok = false;
         break;
@@ -551,11 +583,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!ok) break;
       mbar_arrive(&p_full[t]);
       ++cnt;
+      have = nhave;
+      j0 = nj0;
+      j1 = nj1;
+      c0 = fmaxf(qsl * nc0, 1e-30f);
+      c1 = fmaxf(qsl * nc1, 1e-30f);
     }
     // epilogue: O / l * v_scale
     uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128;
     if (ok && cnt > 0) {
-      if (mbar_wait_warp(o_full, 0u, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
+      if (mbar_wait_warp(&o_full[t], 0u, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         tc_fence_after();
         __syncwarp();
         const float inv_l = l > 0.f ? 1.0f / l : 0.f;
