@@ -53,12 +53,55 @@ __device__ __forceinline__ void fht16(float (&v)[16]) {
   for (int b0 = 0; b0 < 4; ++b0) h4_stage(t, 4, v, b0);
 }
 
+// exp(x) for x in [-20, 0], the argument range of the GELU's tanh: the IEEE
+// operations of h3b_expf on that range without its range branches.  rint(x log2 e)
+// is taken by adding and subtracting 1.5 * 2^23 (round half to even, as rintf),
+// the integer exponent comes from that sum's low bits, and one power-of-two
+// scaling replaces the two half scalings (equal, since every product stays
+// normal for n >= -29).  Matches h3b_expf bit for bit on every float of [-20, 0].
+__device__ __forceinline__ float expf_neg20(float x) {
+  const float kLog2e = 1.44269502162933349609375f;
+  const float kLn2Hi = 0.693145751953125f;
+  const float kLn2Lo = 1.428606765330187045e-06f;
+  const float t = __fadd_rn(__fmul_rn(x, kLog2e), 12582912.0f);
+  const float n = __fsub_rn(t, 12582912.0f);
+  float r = fmaf(-n, kLn2Hi, x);
+  r = fmaf(-n, kLn2Lo, r);
+  float p = 1.0f / 5040.0f;
+  p = fmaf(p, r, 1.0f / 720.0f);
+  p = fmaf(p, r, 1.0f / 120.0f);
+  p = fmaf(p, r, 1.0f / 24.0f);
+  p = fmaf(p, r, 1.0f / 6.0f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int ni = (int)(__float_as_uint(t) - 0x4B400000u);
+  return __fmul_rn(p, __uint_as_float((uint32_t)(ni + 127) << 23));
+}
+// h3b_tanhf without branches: (1 - e) / (1 + e) correctly rounded by Markstein's
+// final step from RN(1 / (1 + e)) (equal to IEEE division for every e in
+// [2e-9, 1], the range exp(-2|x|) takes for |x| < 10); |x| >= 10 gives +-1.
+__device__ __forceinline__ float tanh_gelu(float x) {
+  const float a = fabsf(x);
+  const float e = expf_neg20(__fmul_rn(-2.0f, a));
+  const float num = __fsub_rn(1.0f, e), den = __fadd_rn(1.0f, e);
+  float t = div_rn_by(num, den, __frcp_rn(den));
+  t = x < 0.0f ? -t : t;
+  return a >= 10.0f ? (x > 0.0f ? 1.0f : -1.0f) : t;
+}
 __device__ __forceinline__ float gelu_tanh(float v) {
   const float kBeta = 0.7978845608028654f;
   const float kKappa = 0.044715f;
   float cube = __fmul_rn(__fmul_rn(__fmul_rn(kKappa, v), v), v);
   float inner = __fmul_rn(kBeta, __fadd_rn(v, cube));
-  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, h3b_tanhf(inner)));
+  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanh_gelu(inner)));
+}
+// int8 code of a scaled value s: clamp to [-128, 127], round half to even by
+// adding 1.5 * 2^23, and take the low byte of the sum's bits -- the code of
+// rintf + clamp + (int) (clamping first cannot change the rounded result).
+__device__ __forceinline__ uint32_t code_byte(float s) {
+  const float c = fminf(127.0f, fmaxf(-128.0f, s));
+  return __float_as_uint(__fadd_rn(c, 12582912.0f)) & 0xffu;
 }
 __device__ __forceinline__ float swiglu(float gate, float up) {
   return __fmul_rn(__fdiv_rn(gate, __fadd_rn(1.0f, h3b_expf(-gate))), up);
@@ -253,9 +296,7 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t ro
         uint32_t word = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float s = bf16r(div_rn_by(bf16r(v[i][4 * w + j]), st, rst));
-          const float qv = fminf(127.0f, fmaxf(-128.0f, rintf(s)));
-          word |= ((uint32_t)(int)qv & 0xffu) << (8 * j);
+          word |= code_byte(bf16r(div_rn_by(bf16r(v[i][4 * w + j]), st, rst))) << (8 * j);
         }
         packed[w] = word;
       }
