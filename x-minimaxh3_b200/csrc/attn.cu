@@ -140,6 +140,13 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// A global load the compiler keeps at this point of the program (it would
+// otherwise sink a read-only load to its first use, behind a barrier wait).
+__device__ __forceinline__ float ld_early(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
 // true in exactly one lane of the (converged) warp
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred;
@@ -568,8 +575,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool nhave = ts.next_pair(nj0, nj1);
       float nc0 = 0.f, nc1 = 0.f;
       if (nhave) {
-        nc0 = __ldg(ksc + nj0);
-        nc1 = nj1 >= 0 ? __ldg(ksc + nj1) : 0.f;
+        nc0 = ld_early(ksc + nj0);
+        nc1 = ld_early(ksc + (nj1 >= 0 ? nj1 : nj0));
       }
       if (!mbar_wait_warp(&s_full[t], (uint32_t)(cnt & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         ok = false;
