@@ -144,59 +144,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-        const int mb = t / num_n, nb = t % num_n;
-        for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
+    // TMA producer: the whole warp runs the loop (warp-uniform control flow),
+    // one elected lane issues the copies
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int mb = t / num_n, nb = t % num_n;
+      for (int kb = 0; kb < num_k; ++kb) {
+        if (!mbar_wait_warp(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
+        if (elect_one()) {
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
           tma_load_2d(sa, &tmA, &full[stage], kb * kBK, mb * kBM);
           tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nb * BN);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
-      }
-      // Drain: every filled stage must have been consumed (its TMA landed and
-      // its MMAs finished) before the CTA may exit.  Bounded like every wait.
-      for (int s = 0; s < kStages; ++s) {
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+        __syncwarp();
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
     }
+    // Drain: every filled stage must have been consumed (its TMA landed and
+    // its MMAs finished) before the CTA may exit.  Bounded like every wait.
+    for (int s2 = 0; s2 < kStages; ++s2) {
+      if (!mbar_wait_warp(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(kBM, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+    // MMA issuer: the whole warp runs the loop (so descriptors stay in uniform
+    // registers), one elected lane issues tcgen05.mma / commit
+    constexpr uint32_t idesc = idesc_i8(kBM, BN);
+    const uint32_t smem_base = smem_u32(smem);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      if (!mbar_wait_warp(&tempty[acc], acc_phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+      bool ok = true;
+      for (int kb = 0; kb < num_k; ++kb) {
+        if (!mbar_wait_warp(&full[stage], phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        bool ok = true;
-        for (int kb = 0; kb < num_k; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
-          const uint32_t sb = sa + S::kABytes;
-          const uint64_t da = sdesc_kmajor_sw128(sa), db = sdesc_kmajor_sw128(sb);
+        const uint32_t sa = smem_base + (uint32_t)(stage * S::kStageBytes);
+        const uint64_t da = sdesc_kmajor_sw128(sa), db = sdesc_kmajor_sw128(sa + S::kABytes);
+        if (elect_one()) {
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
             // +32 bytes of K per MMA: +2 in the descriptor's 16-byte address units
             mma_i8_ss(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
-        if (!ok) break;
-        mma_commit(&tfull[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
+      if (!ok) break;
+      if (elect_one()) mma_commit(&tfull[acc]);
+      __syncwarp();
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   } else {
     // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
