@@ -104,6 +104,24 @@ def test_gemm_i32_full_size_vs_cublas(ops):
     assert torch.equal(acc, ref)
 
 
+@pytest.mark.parametrize("m,n,k", [(2222, 4160, 2048), (4100, 4096, 4224)])
+def test_gemm_pair_kernel_bit_exact(ops, m, n, k):
+    """Shapes with at least one 256-row pair tile per SM run the 2-SM kernel
+    (tcgen05.mma.cta_group::2): its int32 accumulators equal cuBLAS's, and its
+    dequant epilogue equals the oracle's epilogue on those accumulators."""
+    g = torch.Generator().manual_seed(m + n + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    ref = torch._int_mm(a, b.t())
+    assert torch.equal(ops.int8_mm_i32(a, b), ref)
+    xs = torch.rand(m, generator=g) * 1e-2 + 1e-4
+    ws = torch.rand(n, generator=g) * 1e-3 + 1e-5
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16)
+    out = ops.int8_linear_prequantized(a, xs.cuda(), b, ws.cuda(), bias.cuda())
+    exp = O.epilogue(ref.cpu().numpy(), xs.numpy(), ws.numpy(), bias.float().numpy())
+    np.testing.assert_array_equal(bits(out), exp)
+
+
 @pytest.mark.parametrize("ws_kind", ["channel", "scalar"])
 @pytest.mark.parametrize("with_bias", [True, False])
 def test_linear_epilogue_bit_exact(ops, ws_kind, with_bias):

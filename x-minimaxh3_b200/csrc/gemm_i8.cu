@@ -3,6 +3,8 @@
 // dequant epilogue fused:  D = bf16(float(acc) * xs[m] * ws[n] + bias[n]),
 // optionally added into a bf16 residual stream with a per-column gate.
 //
+// Two kernels.  Large problems (at least one 256 x 256 tile per SM) run the
+// 2-SM kernel at the end of this file; the rest run this 1-SM kernel.
 // Persistent, warp-specialized CTA (192 threads, one CTA per SM):
 //   warp 0      TMA producer: A [128 x 128 B] and B [BN x 128 B] tiles into a
 //               kStages-deep shared-memory ring (128-byte swizzle, no multicast)
@@ -244,6 +246,193 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ 2-SM variant
+// A cluster of two CTAs on two SMs computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2 (M 256, N 256, K 32): each CTA loads its own 128 rows
+// of A and one half (128 rows) of the B tile into its own shared memory, and the
+// even CTA's MMA reads both CTAs' operands.  Per 128-deep K step an SM then reads
+// 32 KB of operands from shared memory instead of the 1-SM kernel's 48 KB, which
+// is what bounds the 1-SM kernel (shared-memory bandwidth, not the tensor pipe).
+// Each CTA's tensor memory holds its 128 rows x 256 columns, two accumulators.
+//   warp 0      TMA producer in both CTAs (no multicast); both signal the even
+//               CTA's full barrier (count 2 + bytes)
+//   warp 1      pair TMEM allocation in both CTAs; MMA issuer in the even CTA,
+//               whose commits arrive on both CTAs' barriers (empty, tfull)
+//   warps 2..5  epilogue in both CTAs; each warp releases the accumulator on the
+//               even CTA's tempty barrier (count 8: 4 warps x 2 CTAs)
+template <int PBN>
+struct PairSmem {
+  static constexpr int kStages = PBN == 256 ? 6 : 8;
+  static constexpr int kABytes = 128 * kBK;
+  static constexpr int kBBytes = (PBN / 2) * kBK;  // this CTA's half of the B tile
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kTotal = kBarOffset + 256 + 1024;
+};
+
+// The pair tile is 256 x PBN; each CTA's tensor memory holds 2 x PBN columns.
+template <int PBN, int KIND>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmArgs a) {
+  using S = PairSmem<PBN>;
+  constexpr int kPairStages = S::kStages;
+  constexpr int kPairABytes = S::kABytes;
+  constexpr int kPairStageBytes = S::kStageBytes;
+  constexpr int kPairBarOffset = S::kBarOffset;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairBarOffset);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;  // [2]
+  uint64_t* tempty = tfull + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int num_m = (a.M + 255) / 256, num_n = (a.N + PBN - 1) / PBN;
+  const int tiles = num_m * num_n;
+  const int num_k = (a.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 2);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * PBN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and the pair's TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  {
+    // the pair allocation must hand both CTAs the same columns; otherwise do no work
+    uint32_t leader_base;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(leader_base) : "r"(mapa_shared(smem_u32(tmem_slot), 0)));
+    if (leader_base != tmem_base) {
+      if (threadIdx.x == 0) record_status(H3B_STATUS_GEMM_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+  __syncthreads();
+  const bool pair_ok = *abort_flag == 0;
+  const uint32_t full0 = mapa_shared(smem_u32(full), 0);
+  const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
+
+  if (warp == 0) {
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; ok && pair_ok && t < tiles; t += pairs) {
+      const int mb = t / num_n, nb = t % num_n;
+      for (int kb = 0; kb < num_k; ++kb) {
+        if (!mbar_wait_warp(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
+        if (elect_one()) {
+          uint8_t* sa = smem + stage * kPairStageBytes;
+          const uint32_t fb = full0 + (uint32_t)(stage * 8);
+          mbar_arrive_expect_tx_cluster(fb, kPairStageBytes);
+          tma_load_2d_pair(sa, &tmA, fb, kb * kBK, mb * 256 + (int)rank * 128);
+          tma_load_2d_pair(sa + kPairABytes, &tmB, fb, kb * kBK, nb * PBN + (int)rank * (PBN / 2));
+        }
+        __syncwarp();
+        if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+      }
+    }
+    // drain: every filled stage consumed before the CTA may exit (bounded)
+    for (int s2 = 0; pair_ok && s2 < kPairStages; ++s2) {
+      if (!mbar_wait_warp(&empty[stage], phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+      if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && pair_ok) {
+      constexpr uint32_t idesc = idesc_i8(256, PBN);
+      const uint32_t smem_base = smem_u32(smem);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = pair; t < tiles; t += pairs) {
+        if (!mbar_wait_warp(&tempty[acc], acc_phase ^ 1, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * PBN);
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait_warp(&full[stage], phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_base + (uint32_t)(stage * kPairStageBytes);
+          const uint64_t da = sdesc_kmajor_sw128(sa), db = sdesc_kmajor_sw128(sa + kPairABytes);
+          if (elect_one()) {
+#pragma unroll
+            for (int k = 0; k < kBK / 32; ++k)
+              mma_i8_ss_pair(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_commit_pair(&empty[stage], 0x3);
+          }
+          __syncwarp();
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (elect_one()) mma_commit_pair(&tfull[acc], 0x3);
+        __syncwarp();
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4) of this CTA's 128 rows
+    const int quad = warp & 3;
+    const int row_in_tile = (int)rank * 128 + quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; pair_ok && t < tiles; t += pairs) {
+      const int mb = t / num_n, nb = t % num_n;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, H3B_STATUS_GEMM_TIMEOUT)) break;
+      tc_fence_after();
+      __syncwarp();
+      const int m = mb * 256 + row_in_tile;
+      const float xs_m = (KIND != kEpiInt32 && m < a.M) ? __ldg(a.xs + m) : 0.0f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * PBN);
+#pragma unroll 1
+      for (int c = 0; c < PBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)(c * 32), r);
+        tmem_wait_ld();
+        if (c == PBN / 32 - 1) {
+          // this warp is done with the accumulator: release it on the even CTA
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
+        }
+        const int n0 = nb * PBN + c * 32;
+        if (m < a.M && n0 < a.N) epi_store_chunk(r, m, n0, a, xs_m, KIND);
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the pair's MMAs and both CTAs' epilogues are done
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * PBN);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -302,8 +491,38 @@ static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, 
   return cudaGetLastError();
 }
 
+constexpr int kPairBN = 256;
+
+template <int KIND>
+static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                                    cudaStream_t s) {
+  auto k = gemm_i8_pair_kernel<kPairBN, KIND>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PairSmem<kPairBN>::kTotal);
+  if (e != cudaSuccess) return e;
+  const int tiles = ((a.M + 255) / 256) * ((a.N + kPairBN - 1) / kPairBN);
+  const int max_pairs = num_sms() / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  k<<<2 * pairs, kGemmThreads, PairSmem<kPairBN>::kTotal, s>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
 // Returns 0 on success, 1 if a tensor map could not be encoded, else a CUDA error.
 int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t s, cudaError_t* err) {
+  if ((int64_t)((a.M + 255) / 256) * ((a.N + kPairBN - 1) / kPairBN) >= num_sms()) {
+    // 2-SM kernel: A rows and B rows in boxes of 128 (each CTA's half of a 256 tile)
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K, kBK,
+                      128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return 1;
+    if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, kBK,
+                      kPairBN / 2, CU_TENSOR_MAP_SWIZZLE_128B))
+      return 1;
+    cudaError_t e = kind == kEpiStore      ? launch_gemm_pair<kEpiStore>(ta, tb, a, s)
+                    : kind == kEpiResidual ? launch_gemm_pair<kEpiResidual>(ta, tb, a, s)
+                                           : launch_gemm_pair<kEpiInt32>(ta, tb, a, s);
+    *err = e;
+    return e == cudaSuccess ? 0 : 2;
+  }
   const int tiles256 = ((a.M + kBM - 1) / kBM) * ((a.N + 255) / 256);
   const int BN = (tiles256 >= num_sms() || a.N > 128) ? 256 : 128;
   CUtensorMap ta, tb;
