@@ -27,6 +27,7 @@
 //               schedule, descriptors in uniform registers, one elected lane
 //               issues): at each of its tile's steps, once the previous P is
 //               written, S(step) and PV(previous step)
+//               P is double-buffered per tile in shared memory.
 //   warps 4..7  softmax of tile A, warps 8..11 of tile B: one query row per
 //               thread (its TMEM lane): S row from TMEM, per-block dequant
 //               scales, online max / sum, P row to shared memory in the
@@ -55,8 +56,8 @@ constexpr int kQBytes = 128 * 128;
 constexpr int kPBytes = 128 * 128;
 constexpr int kKVBytes = 32768;  // K pair 16 KB + V^T pair 2 x 8 KB
 constexpr int kOffQ = 0;                          // 2 tiles
-constexpr int kOffP = kOffQ + 2 * kQBytes;        // 2 tiles
-constexpr int kOffKV = kOffP + 2 * kPBytes;
+constexpr int kOffP = kOffQ + 2 * kQBytes;        // 2 tiles x 2 buffers
+constexpr int kOffKV = kOffP + 4 * kPBytes;
 constexpr int kOffBar = kOffKV + kKVStages * kKVBytes;
 constexpr int kAttnSmem = kOffBar + 256 + 1024;
 constexpr float kLog2_112 = 6.807354922057604f;
@@ -293,7 +294,9 @@ __device__ __forceinline__ void rebias_s(uint32_t s_addr) {
 // maximum is taken.  The running max m moves (to the tile max) only when the
 // tile max exceeds it by more than kTau; then O is rescaled.  cnt = steps this
 // tile already processed: the PV of step cnt - 1 may still be running and is
-// waited for, on pv_done, only before O is rescaled or P is overwritten.
+// waited for, on pv_done, only before O is rescaled.  P is double-buffered: the
+// buffer written here was last read by the PV of step cnt - 2, which the MMA
+// warp issued before this step's S, so it completed before S did.
 template <int NC>
 __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint8_t* prow, int r, float c0,
                                              float c1, int n0, int n1, int cnt, float& m, float& l,
@@ -318,13 +321,11 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
   }
   const float m_new = tmax > m + kTau ? tmax : m;
   float alpha = 1.f;
-  bool pv_waited = false;
   if (__any_sync(0xffffffffu, m_new != m)) {
     alpha = ex2(m - m_new);
     m = m_new;
     if (cnt > 0) {
       if (!mbar_wait_warp(pv_done, (uint32_t)((cnt - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
-      pv_waited = true;
       tc_fence_after();
       __syncwarp();
 #pragma unroll 1
@@ -342,9 +343,6 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
   const float off = kLog2_112 - m;
   float psum = exp_block<0>(s, c0, off - kMagicF * c0);
   if constexpr (NC == 128) psum += exp_block<64>(s, c1, off - kMagicF * c1);
-  if (cnt > 0 && !pv_waited) {
-    if (!mbar_wait_warp(pv_done, (uint32_t)((cnt - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
-  }
   store_p<NC>(s, prow, r);
   tmem_wait_st();
   fence_proxy_async_smem();
@@ -465,7 +463,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool ok = mbar_wait_warp(q_full, 0, abort_flag, H3B_STATUS_ATTN_TIMEOUT);
     constexpr uint32_t idesc_pv = idesc_e4m3(128, 128);
     const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ + t * kQBytes));
-    const uint32_t pbase = smem_u32(smem + kOffP + t * kPBytes);
+    const uint32_t pbase0 = smem_u32(smem + kOffP + 2 * t * kPBytes);  // P buffer of this tile's even steps
     const uint32_t kv_addr = smem_u32(smem + kOffKV);
     const uint32_t s_tmem = tmem + (uint32_t)(t * 128);
     const uint32_t o_tmem = tmem + 256 + (uint32_t)(t * 128);
@@ -473,6 +471,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint32_t phase = 0;
     int pst = -1;          // stage of the pending PV (-1: none)
     bool ptwo = false, first = true;
+    uint32_t pbuf = 0;     // P buffer of the pending PV
     uint32_t ppar = 0;     // parity of the next p_full phase
     auto wait_p = [&]() -> bool {
       if (!mbar_wait_warp(&p_full[t], ppar, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
@@ -482,6 +481,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     };
     auto issue_pv = [&]() {
       const uint32_t vbase = kv_addr + (uint32_t)(pst * kKVBytes + 16384);
+      const uint32_t pbase = pbase0 + pbuf * (uint32_t)kPBytes;
       if (elect_one()) {
         mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase), sdesc_kmajor_sw64(vbase), idesc_pv, first ? 0u : 1u);
         mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 32), sdesc_kmajor_sw64(vbase + 32), idesc_pv, 1u);
@@ -495,6 +495,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       first = false;
       pst = -1;
+      pbuf ^= 1u;
     };
     int j0, j1, who;
     while (ok && it.next(j0, j1, who)) {
@@ -543,7 +544,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + (uint32_t)(t * 128);
     const uint32_t o_addr = tmem + lane_off + 256 + (uint32_t)(t * 128);
-    uint8_t* prow = smem + kOffP + t * kPBytes + r * 128;
+    uint8_t* prow0 = smem + kOffP + 2 * t * kPBytes + r * 128;
     const float* ksc = a.k_scale + (int64_t)h * a.Kb;
     TileStream ts;
     ts.init(a, h, qta + t, t == 0 || has_b);
@@ -576,6 +577,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       tc_fence_after();
+      uint8_t* prow = prow0 + (cnt & 1) * kPBytes;
       ok = two ? softmax_step<128>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
                                    abort_flag)
                : softmax_step<64>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
