@@ -155,16 +155,25 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
   }
 
   float pp[4] = {0.f, 0.f, 0.f, 0.f}, sp[4] = {0.f, 0.f, 0.f, 0.f}, amax = 0.f;
+#pragma unroll 4
   for (int r = warp; r < valid; r += 4) {
     float v[4];
     load4_row(a, r0 + r, h, lane, mean4, v);
     float sq = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])), __fmul_rn(v[2], v[2])),
                          __fmul_rn(v[3], v[3]));
     const float norm = __fsqrt_rn(warp_butterfly_sum(sq));
+    // v / norm correctly rounded: Markstein's final step from RN(1/norm) where
+    // every quotient that survives the f16 rounding keeps an exact residual
+    // (norm >= 2^-60); IEEE division for tiny, zero, infinite or NaN norms
+    const bool markstein = norm >= 8.673617379884035e-19f && norm <= 3.4e38f;
+    const float rn = __frcp_rn(norm);
+    float qn[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qn[i] = markstein ? div_rn_by(v[i], norm, rn) : __fdiv_rn(v[i], norm);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       pp[i] = __fadd_rn(pp[i], v[i]);
-      sp[i] = __fadd_rn(sp[i], f16r(__fdiv_rn(v[i], norm)));
+      sp[i] = __fadd_rn(sp[i], f16r(qn[i]));
       amax = fmaxf(amax, fabsf(v[i]));
     }
   }
@@ -202,6 +211,10 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
   }
   __syncthreads();
   const float sc = scale_s;
+  // v / sc by Markstein's final step from RN(1/sc): sc >= 1e-7, and the codes
+  // depend only on quotients of magnitude >= 0.5, where its residual is exact
+  const float rsc = __frcp_rn(sc);
+#pragma unroll 4
   for (int r = warp; r < a.blk; r += 4) {
     uint32_t word = 0;
     if (r < valid) {
@@ -209,7 +222,7 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
       load4_row(a, r0 + r, h, lane, mean4, v);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float t = __fdiv_rn(v[i], sc);
+        float t = div_rn_by(v[i], sc, rsc);
         t = __fadd_rn(t, t >= 0.0f ? 0.5f : -0.5f);
         float tr = fminf(127.0f, fmaxf(-127.0f, truncf(t)));
         word |= ((uint32_t)(int)tr & 0xffu) << (8 * i);
@@ -228,58 +241,82 @@ cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s) {
 
 // ------------------------------------------------------------------ q/k RMSNorm + RoPE
 
-// One warp per (token, q|k, head), in place on the projection output rows:
+// In place on the projection output rows, per (token, q|k, head):
 // n = bf16((x * inv_rms) * w);  for d < rot/2 with its partner e = d + rot/2:
 //   out_d = bf16(n_d cos - n_e sin), out_e = bf16(n_d sin + n_e cos)
 // (model/layers.py:72-149 split-half partial RoPE after per-head RMSNorm).
+// One warp per (token, q|k): lane l owns channels 4l..4l+3 of every head, loads
+// its cos/sin values once and walks the heads four at a time, so four
+// independent reductions are in flight.
+__device__ __forceinline__ void load4_bf16(const uint16_t* p, bool vec, float (&v)[4]) {
+  if (vec) {
+    const uint2 r = *reinterpret_cast<const uint2*>(p);
+    v[0] = __uint_as_float(r.x << 16);
+    v[1] = __uint_as_float(r.x & 0xffff0000u);
+    v[2] = __uint_as_float(r.y << 16);
+    v[3] = __uint_as_float(r.y & 0xffff0000u);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bf16_bits_to_f32(p[i]);
+  }
+}
+
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(QkRopeArgs a) {
   const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const int64_t per_tok = 2 * (int64_t)a.H;
-  if (wid >= a.L * per_tok) return;
-  const int64_t t = wid / per_tok;
-  const int rem = (int)(wid % per_tok);
-  const bool is_k = rem >= a.H;
-  const int h = is_k ? rem - a.H : rem;
-  uint16_t* p = a.x + t * a.stride + (is_k ? a.k_off : a.q_off) + (int64_t)h * kD + 4 * lane;
-  const uint16_t* w = (is_k ? a.kw : a.qw) + 4 * lane;
-  const uint2 raw = *reinterpret_cast<const uint2*>(p);
-  const uint2 wr = *reinterpret_cast<const uint2*>(w);
-  float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u), __uint_as_float(raw.y << 16),
-                __uint_as_float(raw.y & 0xffff0000u)};
-  const float wv[4] = {__uint_as_float(wr.x << 16), __uint_as_float(wr.x & 0xffff0000u),
-                       __uint_as_float(wr.y << 16), __uint_as_float(wr.y & 0xffff0000u)};
-  const float sq = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])), __fmul_rn(v[2], v[2])),
-                             __fmul_rn(v[3], v[3]));
-  const float ss = warp_butterfly_sum(sq);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
-  float n[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) n[i] = bf16r(__fmul_rn(__fmul_rn(v[i], inv), wv[i]));
+  if (wid >= 2 * a.L) return;
+  const int64_t t = wid >> 1;
+  const bool is_k = (wid & 1) != 0;
+  uint16_t* row = a.x + t * a.stride + (is_k ? a.k_off : a.q_off) + 4 * lane;
+  float wv[4];
+  load4_bf16((is_k ? a.kw : a.qw) + 4 * lane, true, wv);
   const int half = a.rot_dim >> 1, d0 = 4 * lane;
   const bool first = d0 < half, rot = d0 < a.rot_dim;
   const int src = first ? lane + (half >> 2) : lane - (half >> 2);
-  float o[4];
+  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (rot) {
+    const int64_t j = t * half + (first ? d0 : d0 - half);
+    const bool vec = ((reinterpret_cast<uintptr_t>(a.cos_t) | reinterpret_cast<uintptr_t>(a.sin_t)) & 7) == 0;
+    load4_bf16(a.cos_t + j, vec, c);
+    load4_bf16(a.sin_t + j, vec, sn);
+  }
+  for (int h0 = 0; h0 < a.H; h0 += 4) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float partner = __shfl_sync(0xffffffffu, n[i], rot ? src : lane);
-    if (rot) {
-      const int j = (first ? d0 : d0 - half) + i;
-      const float c = bf16_bits_to_f32(a.cos_t[t * half + j]);
-      const float s = bf16_bits_to_f32(a.sin_t[t * half + j]);
-      o[i] = first ? bf16r(__fsub_rn(__fmul_rn(n[i], c), __fmul_rn(partner, s)))
-                   : bf16r(__fadd_rn(__fmul_rn(partner, s), __fmul_rn(n[i], c)));
-    } else {
-      o[i] = n[i];
+    for (int u = 0; u < 4; ++u) {
+      const int h = h0 + u;
+      if (h >= a.H) break;  // uniform across the warp
+      uint16_t* p = row + (int64_t)h * kD;
+      const uint2 raw = *reinterpret_cast<const uint2*>(p);
+      const float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                          __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u)};
+      const float sq = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])),
+                                           __fmul_rn(v[2], v[2])),
+                                 __fmul_rn(v[3], v[3]));
+      const float ss = warp_butterfly_sum(sq);
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
+      float n[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) n[i] = bf16r(__fmul_rn(__fmul_rn(v[i], inv), wv[i]));
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float partner = __shfl_sync(0xffffffffu, n[i], rot ? src : lane);
+        if (rot) {
+          o[i] = first ? bf16r(__fsub_rn(__fmul_rn(n[i], c[i]), __fmul_rn(partner, sn[i])))
+                       : bf16r(__fadd_rn(__fmul_rn(partner, sn[i]), __fmul_rn(n[i], c[i])));
+        } else {
+          o[i] = n[i];
+        }
+      }
+      *reinterpret_cast<uint2*>(p) =
+          make_uint2((uint32_t)f32_to_bf16_bits(o[0]) | ((uint32_t)f32_to_bf16_bits(o[1]) << 16),
+                     (uint32_t)f32_to_bf16_bits(o[2]) | ((uint32_t)f32_to_bf16_bits(o[3]) << 16));
     }
   }
-  *reinterpret_cast<uint2*>(p) =
-      make_uint2((uint32_t)f32_to_bf16_bits(o[0]) | ((uint32_t)f32_to_bf16_bits(o[1]) << 16),
-                 (uint32_t)f32_to_bf16_bits(o[2]) | ((uint32_t)f32_to_bf16_bits(o[3]) << 16));
 }
 
 cudaError_t launch_qk_rmsnorm_rope(const QkRopeArgs& a, cudaStream_t s) {
-  const int64_t warps = a.L * 2 * a.H;
+  const int64_t warps = a.L * 2;
   qk_rmsnorm_rope_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a);
   return cudaGetLastError();
 }

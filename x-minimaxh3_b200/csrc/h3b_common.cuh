@@ -79,6 +79,15 @@ __device__ __forceinline__ float h3b_tanhf(float x) {
   return x < 0.0f ? -t : t;
 }
 
+// Correctly rounded a / b from rb = RN(1/b) (Markstein: q = RN(a*rb) is within
+// one ulp, the residual a - b*q is exact through one fma, and q + residual*rb
+// rounds to RN(a/b) when no underflow or overflow occurs).
+__device__ __forceinline__ float div_rn_by(float a, float b, float rb) {
+  const float q = __fmul_rn(a, rb);
+  const float r = fmaf(-q, b, a);
+  return fmaf(r, rb, q);
+}
+
 // Butterfly sum over a warp (every lane ends with the same bits).
 __device__ __forceinline__ float warp_butterfly_sum(float v) {
 #pragma unroll

@@ -35,14 +35,6 @@ __device__ __forceinline__ void h4_stage(const float* x, int s, float* y, int ba
   y[base + 2 * s] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(d01, x2), x3));
   y[base + 3 * s] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(x2, d01), x3));
 }
-// Correctly rounded a / b from rb = RN(1/b) (Markstein: q = RN(a*rb) is within
-// one ulp, the residual a - b*q is exact through one fma, and q + residual*rb
-// rounds to RN(a/b) when no underflow or overflow occurs).
-__device__ __forceinline__ float div_rn_by(float a, float b, float rb) {
-  const float q = __fmul_rn(a, rb);
-  const float r = fmaf(-q, b, a);
-  return fmaf(r, rb, q);
-}
 
 // Two radix-4 stages (stride 1 then 4) over 16 values held by one thread.
 __device__ __forceinline__ void fht16(float (&v)[16]) {
