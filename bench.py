@@ -36,6 +36,11 @@ METRIC = "H3 DiT block tokens/s @720p5s INT8/W4A8; GEMM & attn % of B200 tensor 
 GRID = (31, 45, 80)  # latent frames x patch rows x patch cols = 111,600 tokens
 
 
+def workload_name(grid) -> str:
+    names = {(31, 45, 80): "720p/5 s", (91, 68, 120): "1080p/15 s"}
+    return "H3-shaped DiT block, " + names.get(tuple(grid), "grid %dx%dx%d" % tuple(grid))
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -43,6 +48,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("h3b", "reference"), default="h3b")
     ap.add_argument("--tokens", type=int, default=0, help="override L (must divide by the GPU count)")
+    ap.add_argument("--grid", type=str, default="", help="latent video grid T,H,W (default 31,45,80 = 720p/5 s; "
+                    "91,68,120 = 1080p/15 s, BASELINE config 5); L is its product unless --tokens is given")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -83,7 +90,7 @@ def run_reference(args, L):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000.0, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32 (dequantized weights, torch CPU)",
-        "data": "synthetic", "config": {"workload": "H3-shaped DiT block, 720p/5 s", "tokens": L,
+        "data": "synthetic", "config": {"workload": workload_name(args.grid_t), "tokens": L,
                                          "hidden": 4096, "heads": 32, "ffn": 16384, "attention": "dense SDPA (CPU)"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info["threads"], "kind": "port",
                          "sample": info["sample"] + "; median of the timed steps"},
@@ -177,7 +184,7 @@ def run_h3b(args, L):
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     x0 = torch.randn(Lp, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
     t = torch.randn(cfg.t_dim, generator=g, device=dev).to(torch.bfloat16)
-    rope = rope_tables(GRID, cfg.rope_splits, start=rank * Lp, count=Lp, device=dev)
+    rope = rope_tables(args.grid_t, cfg.rope_splits, start=rank * Lp, count=Lp, device=dev)
     x = torch.empty_like(x0)
 
     # instrument the dominant kernel (the quantized attention) with CUDA events
@@ -298,7 +305,10 @@ def run_h3b(args, L):
         prof = os.path.join(ROOT, "profiles", "attn_traffic.json")
         if os.path.exists(prof):
             try:
-                traffic = json.load(open(prof)).get("bytes_per_launch_scaled")
+                prof_d = json.load(open(prof))
+                # the capture is scaled to the default workload's launch only
+                if L == GRID[0] * GRID[1] * GRID[2] and world == 1:
+                    traffic = prof_d.get("bytes_per_launch_scaled")
             except (OSError, ValueError):
                 traffic = None
         density = attn_ops_launch / (4.0 * 128 * 64 * 128 * math.ceil(pq.tokens / 128) * math.ceil(pk.tokens / 64)
@@ -308,8 +318,8 @@ def run_h3b(args, L):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 (W8A8 / W4A8 GEMMs), int8-QK / fp8-PV attention",
             "data": "synthetic (N(0,1) hidden states, random-init H3-format weights)",
-            "config": {"workload": "H3-shaped DiT block, 720p/5 s (BASELINE configs 1-4 combined in one block)",
-                       "tokens": L, "grid": list(GRID), "hidden": cfg.hidden, "heads": cfg.heads,
+            "config": {"workload": workload_name(args.grid_t) + " (BASELINE configs 1-4 combined in one block)",
+                       "tokens": L, "grid": list(args.grid_t), "hidden": cfg.hidden, "heads": cfg.heads,
                        "ffn": cfg.ffn, "mlp": f"W4A8 G={cfg.w4_group} {cfg.mlp_act}",
                        "attention": f"Sparge {cfg.mask.mode} {cfg.mask.budget} + first column + diagonal",
                        "kept_tile_fraction": round(density, 4),
@@ -339,7 +349,10 @@ def run_h3b(args, L):
 
 def main():
     args = parse()
-    L = args.tokens or GRID[0] * GRID[1] * GRID[2]
+    args.grid_t = tuple(int(v) for v in args.grid.split(",")) if args.grid else GRID
+    if len(args.grid_t) != 3 or min(args.grid_t) <= 0:
+        raise SystemExit("--grid takes three positive integers T,H,W")
+    L = args.tokens or args.grid_t[0] * args.grid_t[1] * args.grid_t[2]
     if args.impl == "reference":
         return run_reference(args, L)
     return run_h3b(args, L)

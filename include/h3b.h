@@ -203,7 +203,7 @@ typedef struct h3b_mask_params {
  * and Q rows kept dense).  pooled_q: bf16 [H, Qb, 128], similar_q: u8 [H, Qb],
  * pooled_k: bf16 [H, Kb, 128], similar_k: u8 [H, Kb].  Output bitmap: uint32
  * [H, Qb, ceil(Kb/32)], bit j%32 of word j/32 set when K block j is kept.
- * Kb <= 8192. */
+ * Kb <= 16384 (1,048,576 key tokens). */
 int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, const void* pooled_k,
                    const void* similar_k, int64_t Kb, int64_t H, const h3b_mask_params* params, void* bitmap,
                    void* stream);

@@ -137,6 +137,19 @@ def test_block_mask_bit_exact(attn, cfg):
     np.testing.assert_array_equal(bm.cpu().numpy().view(np.uint32), ref)
 
 
+def test_block_mask_bit_exact_beyond_8192_key_blocks(attn):
+    """8208 key blocks (525,295 keys, the 4-rows-per-CTA kernel): bit-exact."""
+    _, pq, pk, _, _ = _prepared_pair(attn, 1000, 1, seed=31, Lk=8208 * 64 - 17)
+    assert pk.scale.shape[1] == 8208
+    mc = attn.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True)
+    bm = attn.block_mask(pq, pk, mc)
+    ref = O.block_mask(bits(pq.pooled), pq.similar.cpu().numpy(), bits(pk.pooled), pk.similar.cpu().numpy(),
+                       mode=1, budget=mc.budget, protected_kb=0, flags=3, temporal_radius=mc.temporal_radius,
+                       temporal_spatial_radius=mc.temporal_spatial_radius, frames=0, frame_tokens=0,
+                       protected_tokens=0, q_tokens=pq.tokens)
+    np.testing.assert_array_equal(bm.cpu().numpy().view(np.uint32), ref)
+
+
 def test_block_mask_reference_selector_golden(attn):
     """Reference fixed-TopK selector (kernels.py:3668-3941) on tie-free inputs."""
     z = np.load(os.path.join(G, "mask_topk.npz"))

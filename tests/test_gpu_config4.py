@@ -1,0 +1,97 @@
+"""BASELINE config 4 at its real length: Sparge attention over L = 219,600 tokens
+(a 61 x 45 x 80 video grid), 128 x 64 blocks (Qb 1716 x Kb 3432), top-CDF 0.6 +
+first column + diagonal.
+
+Q and K are a rank-16 smooth field over (t, h, w) plus 0.3 N(0, 1) noise: 16
+random separable cosine modes, projected to the head dimension by a [16, 128]
+N(0, 1/16) matrix per head; V is N(0, 1).  Two heads keep the CPU oracle's
+share of the test to seconds.  Checked:
+  * the block bitmap equals the CPU oracle's selector bit for bit;
+  * the attention output of three sampled query tiles (first, middle, last)
+    is within cos >= 0.999 / rel-L2 <= 3e-2 of fp32 attention over the same
+    dequantized operands restricted to the selected blocks (the tolerance of
+    the other attention tests);
+  * no bounded wait timed out.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import bits, cosine, rel_l2
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GRID = (61, 45, 80)
+H = 2
+
+
+def smooth_field(grid, heads, gen):
+    T, Y, X = grid
+    axes = [torch.arange(n, dtype=torch.float32) for n in grid]
+    modes = []
+    for _ in range(16):
+        f = torch.rand(3, generator=gen) * 4.0          # cycles over each extent
+        p = torch.rand(3, generator=gen) * 2 * math.pi
+        c = [torch.cos(2 * math.pi * f[i] * axes[i] / grid[i] + p[i]) for i in range(3)]
+        modes.append((c[0][:, None, None] * c[1][None, :, None] * c[2][None, None, :]).reshape(-1))
+    field = torch.stack(modes, 1)                        # [L, 16]
+    proj = torch.randn(heads, 16, 128, generator=gen) / 4.0
+    x = torch.einsum("lm,hmd->lhd", field, proj)
+    return (x + 0.3 * torch.randn(x.shape, generator=gen)).to(torch.bfloat16)
+
+
+def sampled_reference(pq, pk, pv, bitmap, tiles):
+    """fp32 attention over the dequantized operands for the query rows of `tiles`."""
+    Lq, Lk = pq.tokens, pk.tokens
+    rows = torch.cat([torch.arange(t * 128, min(Lq, t * 128 + 128)) for t in tiles]).cuda()
+    qs = pq.scale.repeat_interleave(pq.block, dim=1)[:, rows]
+    ks = pk.scale.repeat_interleave(64, dim=1)[:, :Lk]
+    q = pq.qi8[:, rows].float() * qs[..., None]
+    k = pk.qi8[:, :Lk].float() * ks[..., None]
+    lut = torch.tensor([O.lib().h3bo_e4m3_to_f32(i) for i in range(256)], device=q.device)
+    v = lut[pv.vt[:, :, :Lk].long()].transpose(1, 2) * pv.scale[:, None, :]
+    s = q @ k.transpose(1, 2) / math.sqrt(128)
+    words = bitmap.view(torch.int32)[:, rows // 128]     # [H, rows, words]
+    Kb = (Lk + 63) // 64
+    keep = ((words[..., :, None] >> torch.arange(32, device=q.device)) & 1).reshape(H, len(rows), -1)[..., :Kb]
+    keep = keep.bool().repeat_interleave(64, 2)[..., :Lk]
+    s = s.masked_fill(~keep, float("-inf"))
+    return (s.softmax(-1) @ v).permute(1, 0, 2), rows
+
+
+def test_config4_sparge_full_length():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import h3b
+    from h3b import attention as A
+
+    gen = torch.Generator().manual_seed(0)
+    q = smooth_field(GRID, H, gen).cuda()
+    k = smooth_field(GRID, H, gen).cuda()
+    v = torch.randn(q.shape, generator=gen).to(torch.bfloat16).cuda()
+    L = q.shape[0]
+    assert L == 219_600
+
+    pk, _ = A.prepare_keys(k)
+    pq = A.prepare_queries(q)
+    pv = A.prepare_values(v)
+    cfg = A.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True)
+    bm = A.block_mask(pq, pk, cfg)
+    assert bm.shape[1] == 1716 and pk.scale.shape[1] == 3432
+
+    ref = O.block_mask(bits(pq.pooled), pq.similar.cpu().numpy(), bits(pk.pooled), pk.similar.cpu().numpy(),
+                       mode=1, budget=cfg.budget, protected_kb=0, flags=3, temporal_radius=cfg.temporal_radius,
+                       temporal_spatial_radius=cfg.temporal_spatial_radius, frames=0, frame_tokens=0,
+                       protected_tokens=0, q_tokens=pq.tokens)
+    np.testing.assert_array_equal(bm.cpu().numpy().view(np.uint32), ref)
+
+    out = A.attention(pq, pk, pv, bm)
+    want, rows = sampled_reference(pq, pk, pv, bm, tiles=(0, 857, 1715))
+    got = out[rows].float()
+    assert cosine(got, want) >= 0.999
+    assert rel_l2(got, want) <= 3e-2
+    assert h3b.device_status(0) == 0

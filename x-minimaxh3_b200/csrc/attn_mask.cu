@@ -19,7 +19,9 @@
 
 namespace h3b {
 
-constexpr int kMaskRows = 8;
+// Query-block rows per CTA: 8, or 4 above 8192 key blocks (the rows' bf16
+// scores are staged in shared memory: rows x Kb x 2 bytes).
+constexpr int kMaskMaxKb = 16384;
 constexpr int kMaskThreads = 256;
 
 
@@ -119,6 +121,7 @@ __device__ int cdf_count(const uint16_t* keys, int Kb, uint64_t thr, uint32_t* h
   return count;
 }
 
+template <int kMaskRows>
 __global__ void __launch_bounds__(kMaskThreads) block_mask_kernel(MaskArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   float* pq_s = reinterpret_cast<float*>(smem);                               // [8][128]
@@ -262,18 +265,24 @@ __global__ void __launch_bounds__(128) bitmap_to_lut_kernel(const uint32_t* __re
   if (lane == 0) valid[row] = n;
 }
 
-size_t mask_smem_bytes(int64_t Kb) {
-  return kMaskRows * 128 * sizeof(float) + kMaskRows * 256 * sizeof(uint32_t) +
-         kMaskRows * 256 * sizeof(unsigned long long) + kMaskRows * (size_t)Kb * sizeof(uint16_t);
+static size_t mask_smem_bytes(int64_t Kb, int rows) {
+  return rows * 128 * sizeof(float) + rows * 256 * sizeof(uint32_t) + rows * 256 * sizeof(unsigned long long) +
+         rows * (size_t)Kb * sizeof(uint16_t);
+}
+
+template <int ROWS>
+static cudaError_t launch_block_mask_rows(const MaskArgs& a, int64_t H, cudaStream_t s) {
+  const size_t smem = mask_smem_bytes(a.Kb, ROWS);
+  cudaError_t e =
+      cudaFuncSetAttribute(block_mask_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((a.Qb + ROWS - 1) / ROWS), (unsigned)H);
+  block_mask_kernel<ROWS><<<grid, kMaskThreads, smem, s>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_block_mask(const MaskArgs& a, int64_t H, cudaStream_t s) {
-  const size_t smem = mask_smem_bytes(a.Kb);
-  cudaError_t e = cudaFuncSetAttribute(block_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((a.Qb + kMaskRows - 1) / kMaskRows), (unsigned)H);
-  block_mask_kernel<<<grid, kMaskThreads, smem, s>>>(a);
-  return cudaGetLastError();
+  return a.Kb <= 8192 ? launch_block_mask_rows<8>(a, H, s) : launch_block_mask_rows<4>(a, H, s);
 }
 
 cudaError_t launch_bitmap_to_lut(const void* bm, int64_t rows, int64_t Kb, void* lut, void* valid, cudaStream_t s) {

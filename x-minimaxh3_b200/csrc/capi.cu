@@ -244,7 +244,7 @@ int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, cons
   if (Qb <= 0 || Kb <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "Qb, Kb and H must be positive");
   if (!pooled_q || !similar_q || !pooled_k || !similar_k || !p || !bitmap || !p->budget)
     return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
-  if (Kb > 8192) return fail(H3B_ERR_UNSUPPORTED, "at most 8192 key blocks");
+  if (Kb > 16384) return fail(H3B_ERR_UNSUPPORTED, "at most 16384 key blocks");
   if (p->mode != 0 && p->mode != 1) return fail(H3B_ERR_INVALID_ARGUMENT, "mode must be 0 or 1");
   h3b::MaskArgs a{static_cast<const uint16_t*>(pooled_q), static_cast<const uint8_t*>(similar_q),
                   static_cast<const uint16_t*>(pooled_k), static_cast<const uint8_t*>(similar_k), Qb, Kb, p->mode,
