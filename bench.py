@@ -14,7 +14,8 @@ attention uses a NCCL all-to-all (tokens -> heads and back).
 
 Prints ONE JSON line on rank 0 (see the keys below).  `value` is device-timed
 with inputs resident in HBM; `e2e` adds the pinned host->device copy of each
-step's hidden states and the device->host read of the result.
+step's hidden states and the device->host read of the result, through
+h3b.block.HostPipeline (the copies of neighbouring steps overlap the block).
 """
 
 from __future__ import annotations
@@ -246,32 +247,28 @@ def run_h3b(args, L):
         ms, attn_ms = float(tmax[0]), float(tmax[1])
     status = h3b.device_status(local)
 
-    # end-to-end: pinned host -> device input, block, device -> host result
+    # end-to-end through the public host-side runner (h3b.block.HostPipeline):
+    # every step copies its hidden states from pinned host memory to the GPU,
+    # runs the block and copies the result back; the copies of neighbouring
+    # steps overlap the block on their own streams
     e2e = None
     if not args.no_e2e:
+        from h3b.block import HostPipeline
         xh = x0.cpu().pin_memory()
         th = t.cpu().pin_memory()
-        out_h = torch.empty_like(xh).pin_memory()
-        xd = torch.empty_like(x0)
-        td = torch.empty_like(t)
-
-        def e2e_step():
-            xd.copy_(xh, non_blocking=True)
-            td.copy_(th, non_blocking=True)
-            block.forward(xd, td, rope)
-            out_h.copy_(xd, non_blocking=True)
-
-        e2e_step()
+        outs = [torch.empty_like(xh).pin_memory() for _ in range(2)]
+        pipe = HostPipeline(block, rope, Lp)
+        pipe.run([xh] * 2, [th] * 2, outs)                      # warm-up
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         s2 = torch.cuda.Event(enable_timing=True)
         e2 = torch.cuda.Event(enable_timing=True)
         s2.record()
-        for _ in range(args.steps):
-            e2e_step()
+        pipe.run([xh] * args.steps, [th] * args.steps, [outs[k % 2] for k in range(args.steps)])
         e2.record()
         torch.cuda.synchronize()
+        out_h = outs[0]
         e2e_ms = s2.elapsed_time(e2) / args.steps
         if world > 1:
             tm = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)

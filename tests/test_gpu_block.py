@@ -114,3 +114,23 @@ def test_sparse_block_runs_and_tracks_dense(blockmod):
     ys = bs.forward(x.clone(), t, rope)
     # a Top-K budget of 1.0 keeps every block: the sparse kernel must equal the dense one
     assert torch.equal(yd, ys)
+
+
+def test_host_pipeline_matches_sequential_forwards(blockmod):
+    """The overlapped host->device / block / device->host runner gives, step for
+    step, the bits of plain forwards on the same inputs."""
+    B = blockmod
+    cfg = B.BlockConfig(hidden=1024, heads=8, ffn=4096, t_dim=256)
+    blk = B.DiTBlockB200(cfg, device="cuda", seed=4)
+    L, steps = 1024, 4
+    g = torch.Generator().manual_seed(6)
+    xs = [torch.randn(L, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory() for _ in range(steps)]
+    ts = [torch.randn(cfg.t_dim, generator=g).to(torch.bfloat16).pin_memory() for _ in range(steps)]
+    outs = [torch.empty(L, cfg.hidden, dtype=torch.bfloat16).pin_memory() for _ in range(steps)]
+    rope = B.rope_tables((4, 16, 16), cfg.rope_splits, device="cuda")
+    pipe = B.HostPipeline(blk, rope, L)
+    pipe.run(xs, ts, outs)
+    torch.cuda.synchronize()
+    for k in range(steps):
+        ref = blk.forward(xs[k].cuda(), ts[k].cuda(), rope).cpu()
+        assert torch.equal(outs[k], ref), k

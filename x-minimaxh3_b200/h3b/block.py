@@ -168,6 +168,71 @@ class DiTBlockB200:
         return 2.0 * tokens * cfg.hidden * (3 * cfg.hidden + cfg.hidden + fc1_out + cfg.ffn)
 
 
+class HostPipeline:
+    """Runs a block over a series of host-resident inputs with the copies hidden.
+
+    Each step copies its hidden states (and timestep vector) from pinned host
+    memory to the GPU, runs the block and copies the result back.  The copies run
+    on their own streams: the host->device copy of step k + 1 and the
+    device->host copy of step k - 1 overlap the block of step k (two device
+    buffers; a buffer is refilled only after the result it held has been read
+    out).  All ordering is by CUDA events; nothing waits on the host.
+    """
+
+    def __init__(self, block: DiTBlockB200, rope: tuple[torch.Tensor, torch.Tensor], tokens: int):
+        dev = block.device
+        self.block, self.rope = block, rope
+        self.x = [torch.empty((tokens, block.cfg.hidden), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+        self.t = [torch.empty((block.cfg.t_dim,), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+        self.s_in = torch.cuda.Stream(device=dev)
+        self.s_out = torch.cuda.Stream(device=dev)
+
+    def run(self, xs_host: list[torch.Tensor], ts_host: list[torch.Tensor], outs_host: list[torch.Tensor]) -> None:
+        """xs_host[k] / ts_host[k] (pinned, bf16) -> outs_host[k] (pinned, bf16), for every k.
+
+        Enqueued on the current stream's timeline: the copies start after the work
+        already on the current stream, and the current stream waits for the last
+        device->host copy, so synchronizing it (or an event recorded on it after
+        this call) makes every output available on the host."""
+        n = len(xs_host)
+        if not (len(ts_host) == n == len(outs_host)):
+            raise ValueError("xs_host, ts_host and outs_host must have the same length")
+        comp = torch.cuda.current_stream(self.block.device)
+        self.s_in.wait_stream(comp)
+        self.s_out.wait_stream(comp)
+        loaded: list[torch.cuda.Event | None] = [None] * n
+        read_out: list[torch.cuda.Event | None] = [None, None]
+
+        def load(k: int) -> None:
+            b = k % 2
+            with torch.cuda.stream(self.s_in):
+                if read_out[b] is not None:
+                    self.s_in.wait_event(read_out[b])
+                self.x[b].copy_(xs_host[k], non_blocking=True)
+                self.t[b].copy_(ts_host[k], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self.s_in)
+                loaded[k] = ev
+
+        if n:
+            load(0)
+        for k in range(n):
+            if k + 1 < n:
+                load(k + 1)
+            b = k % 2
+            comp.wait_event(loaded[k])
+            self.block.forward(self.x[b], self.t[b], self.rope)
+            done = torch.cuda.Event()
+            done.record(comp)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(done)
+                outs_host[k].copy_(self.x[b], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self.s_out)
+                read_out[b] = ev
+        comp.wait_stream(self.s_out)
+
+
 def kept_tiles(bitmap: torch.Tensor, key_tokens: int) -> int:
     """Number of kept (Q block, K block) tiles in a bitmap (bits beyond Kb are zero)."""
     b = bitmap.view(torch.int32)
