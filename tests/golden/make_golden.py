@@ -1,7 +1,7 @@
 """Generate golden vectors from the reference's own importable Python code.
 
-Run once in a container that has the X-MinimaxH3 sources (read-only) at
-REFERENCE_ROOT (default /root/reference); the resulting *.npz fixtures are
+Run once in a container that has the X-MinimaxH3 sources (read-only), passing
+their location as the first argument or in REFERENCE_ROOT; the resulting *.npz fixtures are
 committed and are the only thing the tests read.  Every fixture records the
 reference function that produced it:
 
