@@ -17,13 +17,18 @@ reference function that produced it:
                       TRITON_INTERPRET=1 (model/sparge_nhd.py:26-227)
   lut.npz             sparse_lut block_map_to_absolute_lut / absolute_lut_to_delta under
                       TRITON_INTERPRET=1 (model/sparse_lut.py:25-74)
+  block_ckpt.npz      assemble_pruned_block + H3TransformerBlock.forward on CPU (no kernels
+                      injected: the ConvRotInt8Linear / ConvRotW4A8Linear float fallbacks,
+                      torch_sdpa attention; model/assembly.py:259-333, layers.py:996-1298) over
+                      the synthetic checkpoint of tests/golden/h3_checkpoint.py, plus each
+                      layer's output on a seeded input and the layer class / spec chosen
   mask_topk.npz       SplitModalityProtectedSpargeAttentionBackend.long_sequence_video_queries
                       (model/kernels.py:3668-3997) with the two absent Sparge helpers replaced
                       by recorders (fill: set the first `count` sorted indices; LUT: capture
                       the final block map), the same injection the reference tests use
                       (tests/native_engine/test_model_optimizations.py:532-569)
 
-Usage:  python tests/golden/make_golden.py [REFERENCE_ROOT]
+Usage:  python tests/golden/make_golden.py [REFERENCE_ROOT [gen_name ...]]
 """
 
 from __future__ import annotations
@@ -298,7 +303,45 @@ def gen_mask():
     del K
 
 
+def gen_block_ckpt():
+    import json
+
+    sys.path.insert(0, OUT)
+    import h3_checkpoint as HC
+    from h3serve.native_engine.model.assembly import MappingTensorSource, assemble_pruned_block
+    from h3serve.native_engine.model.config import H3CoreConfig
+    from h3serve.native_engine.model.layers import torch_sdpa
+    from h3serve.native_engine.model.lora import AdaLNCurveRows
+
+    state, metadata, inputs = HC.synthetic_block(0)
+    cfg = H3CoreConfig(hidden_size=HC.HIDDEN, num_heads=HC.HEADS, head_dim=HC.HEAD_DIM, ffn_size=HC.FFN,
+                       num_layers=1)
+    source = MappingTensorSource(state, quantization_metadata=metadata)
+    block = assemble_pruned_block(0, source, config=cfg, device="cpu", compute_dtype=torch.bfloat16,
+                                  attention_backend=torch_sdpa)
+    names = {"qkv": "attn.qkv_proj", "out": "attn.out_proj", "fc1": "mlp.fc1", "fc2": "mlp.fc2"}
+    modules = {"qkv": block.attention.qkv_proj, "out": block.attention.out_proj, "fc1": block.mlp.fc1,
+               "fc2": block.mlp.fc2}
+    g = torch.Generator().manual_seed(11)
+    arrays, chosen = {}, {}
+    with torch.no_grad():
+        for tag, mod in modules.items():
+            xin = torch.randn(32, mod.in_features, generator=g).to(torch.bfloat16)
+            arrays[f"layer_{tag}_x"] = bits(xin)
+            arrays[f"layer_{tag}_out"] = bits(mod(xin))
+            spec = mod.spec
+            chosen[names[tag]] = {"class": type(mod).__name__,
+                                  "spec": {k: getattr(spec, k) for k in spec.__slots__}}
+        rows = AdaLNCurveRows(compressed=inputs["curve_rows"], full_silu=None)
+        out = block(inputs["x"].clone(), timestep_rows=rows, modulation_segments=inputs["segments"],
+                    frequencies=inputs["frequencies"])
+    save("block_ckpt.npz", out=bits(out), x=bits(inputs["x"]), digest=np.array(HC.state_digest(state)),
+         chosen=np.array(json.dumps(chosen, sort_keys=True)), **arrays)
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
-    for fn in (gen_quant, gen_convrot, gen_act, gen_w4, gen_linear, gen_sparge, gen_lut, gen_mask):
-        fn()
+    only = sys.argv[2:]
+    for fn in (gen_quant, gen_convrot, gen_act, gen_w4, gen_linear, gen_sparge, gen_lut, gen_mask, gen_block_ckpt):
+        if not only or fn.__name__ in only:
+            fn()

@@ -37,21 +37,11 @@ def _rot(x, h):
     return torch.matmul(x.reshape(-1, x.shape[-1] // 256, 256), h).reshape_as(x)
 
 
-def _decode_w4(packed, s_rel, s_ch, group):
-    p = packed.to(torch.int32) & 0xFF
-    codes = torch.empty(p.shape[0], p.shape[1] * 2, dtype=torch.int32, device=p.device)
-    codes[:, 0::2] = p & 0xF
-    codes[:, 1::2] = (p >> 4) & 0xF
-    n, k = codes.shape
-    grid = ((codes.float() - 8).view(n, k // group, group) * s_rel.unsqueeze(-1)).round().clamp(-127, 127)
-    return (grid * s_ch.view(-1, 1, 1)).reshape(n, k)
-
-
 def reference_block(blk, x, t, rope):
     cfg = blk.cfg
     H, D = cfg.heads, cfg.head_dim
     hm = _had(x.device)
-    mod = blk.modulation(t).float()
+    mod = blk.modulation(t).float()[0]
     sa, ca, ga, sm, cm, gm = mod.unbind(0)
 
     def rms_adaln(v, w, scale, shift):
@@ -60,7 +50,7 @@ def reference_block(blk, x, t, rope):
 
     xf = x.float()
     h = rms_adaln(xf, blk.norm1, ca, sa)
-    qkv = F.linear(_rot(h, hm), blk.w_qkv.float() * blk.s_qkv[:, None], blk.b_qkv.float())
+    qkv = F.linear(_rot(h, hm), blk.qkv.dense_weight(), blk.qkv.bias.float())
     L = x.shape[0]
     q, k, v = qkv.view(L, 3, H, D).unbind(1)
     cos, sin = rope[0].float(), rope[1].float()
@@ -74,12 +64,10 @@ def reference_block(blk, x, t, rope):
     q, k = norm_rope(q, blk.q_norm), norm_rope(k, blk.k_norm)
     o = torch.softmax(torch.einsum("lhd,mhd->hlm", q, k) / math.sqrt(D), -1)
     o = torch.einsum("hlm,mhd->lhd", o, v).reshape(L, H * D)
-    xf = xf + F.linear(_rot(o, hm), blk.w_o.float() * blk.s_o[:, None], blk.b_o.float()) * ga
+    xf = xf + F.linear(_rot(o, hm), blk.out.dense_weight(), blk.out.bias.float()) * ga
     h = rms_adaln(xf, blk.norm2, cm, sm)
-    w1 = _decode_w4(*blk.fc1, cfg.w4_group)
-    u = F.gelu(F.linear(_rot(h, hm), w1, blk.b_fc1.float()), approximate="tanh")
-    w2 = _decode_w4(*blk.fc2, cfg.w4_group)
-    return xf + F.linear(_rot(u, hm), w2, blk.b_fc2.float()) * gm
+    u = F.gelu(F.linear(_rot(h, hm), blk.fc1.dense_weight(), blk.fc1.bias.float()), approximate="tanh")
+    return xf + F.linear(_rot(u, hm), blk.fc2.dense_weight(), blk.fc2.bias.float()) * gm
 
 
 @pytest.mark.parametrize("L", [1536, 2000])

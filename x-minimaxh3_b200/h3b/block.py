@@ -27,6 +27,7 @@ import torch
 from . import attention as A
 from . import ops
 from . import parallel as P
+from . import quantization as Q
 
 
 @dataclass
@@ -65,6 +66,39 @@ def _int4_grouped(w: torch.Tensor, group: int) -> tuple[torch.Tensor, torch.Tens
     return packed.contiguous(), (gscale / cscale.unsqueeze(-1)).float().contiguous(), cscale.float().contiguous()
 
 
+def _runs(segments, rows: int, table_rows: int):
+    """Validated AdaLN runs ((start, stop, row), ...) or None for row 0 everywhere."""
+    if segments is None:
+        return None
+    runs, prev = [], 0
+    for start, stop, row in segments:
+        start, stop, row = int(start), int(stop), int(row)
+        if start != prev or stop <= start:
+            raise ValueError("modulation segments must be an ordered partition")
+        if not 0 <= row < table_rows:
+            raise ValueError(f"modulation row {row} outside the {table_rows} AdaLN rows")
+        runs.append((start, stop, row))
+        prev = stop
+    if prev != rows:
+        raise ValueError("modulation segments do not cover the packed sequence")
+    return runs
+
+
+def rope_tables_from_frequencies(frequencies: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(cos, sin) bf16 [L, rot/2] tables from the engine's RoPE input: split-half angles
+    [L, rot] (model/layers.py:51-57) or the packed rotation table [1, L, 1, rot/2, 2, 2]
+    (model/layers.py:60-69).  The angle form takes cos/sin in fp32 and rounds to bf16,
+    as the engine's unfused path does (model/layers.py:137-140)."""
+    if frequencies.dim() == 6:
+        table = frequencies[0, :, 0]
+        return table[..., 0, 0].to(torch.bfloat16).contiguous(), table[..., 1, 0].to(torch.bfloat16).contiguous()
+    if frequencies.dim() != 2 or frequencies.shape[1] % 2:
+        raise ValueError("frequencies must be angles [L, rot] or a rotation table [1, L, 1, rot/2, 2, 2]")
+    half = frequencies.shape[1] // 2
+    active = frequencies[:, :half].float()
+    return torch.cos(active).to(torch.bfloat16).contiguous(), torch.sin(active).to(torch.bfloat16).contiguous()
+
+
 def rope_tables(grid: tuple[int, int, int], splits=(44, 42, 42), theta: float = 10000.0, start: int = 0,
                 count: int | None = None, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
     """Split-half 3-D RoPE tables (cos, sin) bf16 [L, sum(splits)/2] for a (t, h, w)
@@ -83,17 +117,17 @@ def rope_tables(grid: tuple[int, int, int], splits=(44, 42, 42), theta: float = 
 
 
 class DiTBlockB200:
-    """One DiT block with random-init H3-format weights on one GPU (or one Ulysses rank)."""
+    """One DiT block on one GPU (or one Ulysses rank).
+
+    The four projections are `h3b.quantization` layers (INT8 or packed W4A8, chosen per
+    layer as the checkpoint records); `DiTBlockB200(cfg)` random-initialises them in the
+    formats BASELINE names (INT8 attention projections, W4A8 MLP) and
+    `h3b.checkpoint.load_block` assembles them from a checkpoint."""
 
     def __init__(self, cfg: BlockConfig, device="cuda", seed: int = 0, group=None):
-        self.cfg = cfg
-        self.device = torch.device(device)
-        self.group = group
-        self.world = torch.distributed.get_world_size(group) if group is not None else 1
-        if cfg.heads % self.world:
-            raise ValueError(f"{cfg.heads} heads do not split over {self.world} ranks")
+        self._setup(cfg, device, group)
         g = torch.Generator(device=self.device).manual_seed(seed)
-        D, F = cfg.hidden, cfg.ffn
+        D, F, W = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim
 
         def randn(*shape, std=1.0):
             return torch.randn(*shape, generator=g, device=self.device) * std
@@ -106,21 +140,59 @@ class DiTBlockB200:
         self.q_norm = (1 + randn(cfg.head_dim, std=0.05)).to(torch.bfloat16)
         self.k_norm = (1 + randn(cfg.head_dim, std=0.05)).to(torch.bfloat16)
         # INT8 linears (ConvRot weights are stored rotated; random weights stand in)
-        self.w_qkv, self.s_qkv = _int8_per_channel(randn(3 * D, D, std=0.02))
-        self.b_qkv = randn(3 * D, std=0.01).to(torch.bfloat16)
-        self.w_o, self.s_o = _int8_per_channel(randn(D, D, std=0.02))
-        self.b_o = randn(D, std=0.01).to(torch.bfloat16)
+        int8 = Q.ComfyQuantSpec("int8_tensorwise", convrot=bool(cfg.convrot), convrot_groupsize=256)
+        w, s = _int8_per_channel(randn(3 * W, D, std=0.02))
+        self.qkv = Q.Int8Linear(w, s, randn(3 * W, std=0.01).to(torch.bfloat16), spec=int8)
+        w, s = _int8_per_channel(randn(D, W, std=0.02))
+        self.out = Q.Int8Linear(w, s, randn(D, std=0.01).to(torch.bfloat16), spec=int8)
+        w4 = Q.W4A8QuantSpec("asym_w4a8_int8", group_size=cfg.w4_group)
         fc1_out = 2 * F if cfg.mlp_act == "swiglu" else F
-        self.fc1 = _int4_grouped(randn(fc1_out, D, std=0.02), cfg.w4_group)
-        self.b_fc1 = randn(fc1_out, std=0.01).to(torch.bfloat16)
-        self.fc2 = _int4_grouped(randn(D, F, std=0.02), cfg.w4_group)
-        self.b_fc2 = randn(D, std=0.01).to(torch.bfloat16)
+        qd, sr, sc = _int4_grouped(randn(fc1_out, D, std=0.02), cfg.w4_group)
+        self.fc1 = Q.W4A8Linear(qd, sr, sc, bias=randn(fc1_out, std=0.01).to(torch.bfloat16), spec=w4)
+        qd, sr, sc = _int4_grouped(randn(D, F, std=0.02), cfg.w4_group)
+        self.fc2 = Q.W4A8Linear(qd, sr, sc, bias=randn(D, std=0.01).to(torch.bfloat16), spec=w4)
+
+    def _setup(self, cfg: BlockConfig, device, group) -> None:
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group
+        self.world = torch.distributed.get_world_size(group) if group is not None else 1
+        if cfg.heads % self.world:
+            raise ValueError(f"{cfg.heads} heads do not split over {self.world} ranks")
         self.last_mask_density: float | None = None
+
+    @classmethod
+    def from_parts(cls, cfg: BlockConfig, *, ada_w, ada_b, norm1, norm2, q_norm, k_norm, qkv, out, fc1, fc2,
+                   device="cuda", group=None) -> "DiTBlockB200":
+        """A block over given weights (bf16 vectors / AdaLN projection, quantization layers)."""
+        blk = cls.__new__(cls)
+        blk._setup(cfg, device, group)
+        blk.ada_w, blk.ada_b = ada_w, ada_b
+        blk.norm1, blk.norm2, blk.q_norm, blk.k_norm = norm1, norm2, q_norm, k_norm
+        blk.qkv, blk.out, blk.fc1, blk.fc2 = qkv, out, fc1, fc2
+        W = cfg.heads * cfg.head_dim
+        fc1_out = 2 * cfg.ffn if cfg.mlp_act == "swiglu" else cfg.ffn
+        shapes = {"qkv": (qkv, 3 * W, cfg.hidden), "out": (out, cfg.hidden, W), "fc1": (fc1, fc1_out, cfg.hidden),
+                  "fc2": (fc2, cfg.hidden, cfg.ffn)}
+        for name, (lin, n, k) in shapes.items():
+            if (lin.out_features, lin.in_features) != (n, k):
+                raise ValueError(f"{name} is [{lin.out_features}, {lin.in_features}], the config needs [{n}, {k}]")
+        if ada_w.shape[0] % (6 * cfg.hidden) or ada_w.shape[1] != cfg.t_dim:
+            raise ValueError("the AdaLN projection must map t_dim to a multiple of 6 * hidden")
+        if fc2.convrot_group_size == 0 and cfg.mlp_act:
+            raise ValueError("the FC2 input activation is fused only into the ConvRot quantizer")
+        return blk
 
     # ------------------------------------------------------------------ stages
     def modulation(self, t: torch.Tensor) -> torch.Tensor:
-        tv = t.float().reshape(-1).to(self.device)
-        return (torch.mv(self.ada_w.float(), tv) + self.ada_b.float()).reshape(6, -1).to(torch.bfloat16)
+        """AdaLN parameters [R, 6, hidden] (shift_a, scale_a, gate_a, shift_m, scale_m, gate_m)
+        from the projection input t [t_dim] or [rows, t_dim].  A projection to 18 * hidden
+        (the H3 checkpoints) gives three modulation rows per input row, selected by
+        `segments` (model/layers.py:910-913)."""
+        w, b = self.ada_w.float(), self.ada_b.float()
+        tf = t.to(self.device).float()
+        out = torch.mv(w, tf.reshape(-1)) + b if tf.dim() == 1 or tf.shape[0] == 1 else tf @ w.T + b
+        return out.reshape(-1, 6, self.cfg.hidden).to(torch.bfloat16)
 
     def attention(self, qkv_heads: torch.Tensor) -> torch.Tensor:
         """qkv_heads: [L, 3*h*128] -> o [L, h, 128] (h heads of this rank)."""
@@ -136,36 +208,49 @@ class DiTBlockB200:
         self._last_attn = (pq, pk, pv, bitmap)
         return A.attention(pq, pk, pv, bitmap)
 
-    def forward(self, x: torch.Tensor, t: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
-        """x: bf16 [L_local, hidden] (updated in place and returned); rope: tables for these tokens."""
+    @staticmethod
+    def _gated(lin, x, gate, q, s, runs) -> None:
+        if runs is None:
+            lin.gated_residual_(x, gate[0], q, s)
+            return
+        for start, stop, row in runs:
+            lin.gated_residual_(x[start:stop], gate[row], q[start:stop], s[start:stop])
+
+    def forward(self, x: torch.Tensor, t: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor],
+                segments=None) -> torch.Tensor:
+        """x: bf16 [L_local, hidden] (updated in place and returned); rope: tables for these
+        tokens; segments: AdaLN runs ((start, stop, row), ...) over x's rows, or None for
+        modulation row 0 everywhere (model/layers.py:916-960)."""
         cfg = self.cfg
-        D = cfg.hidden
         mod = self.modulation(t)
-        shift_a, scale_a, gate_a, shift_m, scale_m, gate_m = mod.unbind(0)
-        xq, xs = ops.rms_adaln_quantize_int8(x, self.norm1, scale_a, shift_a, None, cfg.eps, cfg.convrot)
-        qkv = ops.int8_linear_prequantized(xq, xs, self.w_qkv, self.s_qkv, self.b_qkv)
-        ops.qk_rmsnorm_rope_(qkv, cfg.heads, 0, D, self.q_norm, self.k_norm, rope[0], rope[1], cfg.qk_eps)
+        shift_a, scale_a, gate_a, shift_m, scale_m, gate_m = mod.unbind(1)
+        runs = _runs(segments, x.shape[0], mod.shape[0])
+        xq, xs = ops.rms_adaln_quantize_int8(x, self.norm1, scale_a, shift_a, segments, cfg.eps,
+                                             self.qkv.convrot_group_size)
+        qkv = self.qkv.forward_prequantized(xq, xs)
+        W = cfg.heads * cfg.head_dim
+        ops.qk_rmsnorm_rope_(qkv, cfg.heads, 0, W, self.q_norm, self.k_norm, rope[0], rope[1], cfg.qk_eps)
         Lp = x.shape[0]
         if self.world > 1:
             o = self.attention(P.tokens_to_heads(qkv, cfg.heads, cfg.head_dim, self.group))
             o2 = P.heads_to_tokens(o.view(o.shape[0], -1), Lp, self.group)
         else:
-            o2 = self.attention(qkv).view(Lp, D)
-        oq, os_ = ops.quantize_int8_rowwise_convrot64(o2, cfg.convrot)
-        ops.int8_linear_gated_residual_(x, gate_a, oq, os_, self.w_o, self.s_o, self.b_o)
-        xq, xs = ops.rms_adaln_quantize_int8(x, self.norm2, scale_m, shift_m, None, cfg.eps, cfg.convrot)
-        w1 = ops.dequant_int4_grouped_to_int8(self.fc1[0], self.fc1[1], None, cfg.w4_group)
-        h = ops.int8_linear_prequantized(xq, xs, w1, self.fc1[2], self.b_fc1)
-        hq, hs = ops.quantize_int8_rowwise_convrot64(h, cfg.convrot, cfg.mlp_act)
-        w2 = ops.dequant_int4_grouped_to_int8(self.fc2[0], self.fc2[1], None, cfg.w4_group)
-        ops.int8_linear_gated_residual_(x, gate_m, hq, hs, w2, self.fc2[2], self.b_fc2)
+            o2 = self.attention(qkv).view(Lp, W)
+        oq, os_ = self.out.quantize(o2)
+        self._gated(self.out, x, gate_a, oq, os_, runs)
+        xq, xs = ops.rms_adaln_quantize_int8(x, self.norm2, scale_m, shift_m, segments, cfg.eps,
+                                             self.fc1.convrot_group_size)
+        h = self.fc1.forward_prequantized(xq, xs)
+        hq, hs = self.fc2.quantize(h, cfg.mlp_act)
+        self._gated(self.fc2, x, gate_m, hq, hs, runs)
         return x
 
     # ------------------------------------------------------------------ accounting
     def linear_ops(self, tokens: int) -> float:
         cfg = self.cfg
+        W = cfg.heads * cfg.head_dim
         fc1_out = 2 * cfg.ffn if cfg.mlp_act == "swiglu" else cfg.ffn
-        return 2.0 * tokens * cfg.hidden * (3 * cfg.hidden + cfg.hidden + fc1_out + cfg.ffn)
+        return 2.0 * tokens * (cfg.hidden * (3 * W + fc1_out) + W * cfg.hidden + cfg.ffn * cfg.hidden)
 
 
 class HostPipeline:

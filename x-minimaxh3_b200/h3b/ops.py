@@ -315,10 +315,18 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     xq, xs = quantize_int8_rowwise_convrot64(x, convrot_groupsize, input_act)
     out = int8_linear_prequantized(xq, xs, w8, s_channel, bias, out_dtype)
     if correction is not None:
-        groups = K // group_size
-        if tuple(correction.shape) != (groups, N):
-            raise ValueError(f"correction must have shape {(groups, N)}, got {tuple(correction.shape)}")
-        # (sum of each group's codes) * xs @ correction, as the reference CUDA path
-        sx = xq.view(-1, groups, group_size).sum(-1, dtype=torch.int32).to(out_dtype) * xs.to(out_dtype)
-        out.addmm_(sx, correction.to(out_dtype))
+        w4a8_group_correction_(out, xq, xs, correction, group_size)
     return out.reshape(*x.shape[:-1], N)
+
+
+def w4a8_group_correction_(out: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, correction: torch.Tensor,
+                           group_size: int) -> torch.Tensor:
+    """out += (sum of each group's activation codes * xs) @ correction [K/G, N], in out's dtype."""
+    M, K = xq.shape
+    groups = K // group_size
+    N = out.shape[-1]
+    if tuple(correction.shape) != (groups, N):
+        raise ValueError(f"correction must have shape {(groups, N)}, got {tuple(correction.shape)}")
+    # (sum of each group's codes) * xs @ correction, as the reference CUDA path
+    sx = xq.view(M, groups, group_size).sum(-1, dtype=torch.int32).to(out.dtype) * xs.reshape(M, 1).to(out.dtype)
+    return out.addmm_(sx, correction.to(out.dtype))
