@@ -268,32 +268,41 @@ float h3bo_tree_sum(const float* v, int n) {
     return r;
 }
 
-/* Threads per row used by the CUDA quantizer: K/16 chunks of 16 columns,
- * rounded up to a warp multiple, at most 512 (thread t owns chunks t, t+T, ...). */
+/* Threads per row used by the CUDA quantizer: 16 per pair of 256-column groups,
+ * rounded up to a warp multiple.  Thread t owns chunk t % 16 (16 columns) of the
+ * groups 2p and 2p + 1, p = t / 16: chunks 32p + t % 16 and 32p + 16 + t % 16. */
 int h3bo_quant_threads(int64_t K) {
     int64_t chunks = K / 16;
-    int64_t T = (chunks + 31) / 32 * 32;
-    return (int)(T > 512 ? 512 : T);
+    int64_t groups = (chunks + 15) / 16;
+    int64_t T = (groups + 1) / 2 * 16;
+    return (int)((T + 31) / 32 * 32);
 }
 
 /* RMSNorm(weight) followed by AdaLN modulation with bf16 materialization after
  * each step (fused_norm_rope.py:12-45; layers.py:916-941):
  *   n = bf16(x * inv_rms * w); n = bf16(n * bf16(1 + scale)); n = bf16(n + bf16(shift)).
  * inv_rms = 1 / sqrt(sum(x^2)/K + eps).  The sum of squares follows the CUDA
- * kernel's fixed order: thread t of T = h3bo_quant_threads(K) adds the squares
- * of its chunks t, t+T, ... (16 columns each, in column order), then the
- * per-thread sums are combined by block_tree_sum. */
+ * kernel's fixed order: thread t of T = h3bo_quant_threads(K) adds the squares of
+ * each of its two chunks in column order (two running sums, zero for a chunk past
+ * the row), adds the two sums, and the per-thread sums are combined by
+ * block_tree_sum. */
 void h3bo_rms_adaln_row(const uint16_t* xr, int64_t K, const uint16_t* w, const uint16_t* scale,
                         const uint16_t* shift, float eps, float* out) {
     int T = h3bo_quant_threads(K);
     int64_t chunks = K / 16;
     float* part = (float*)calloc(1024, sizeof(float));
-    for (int t = 0; t < T; ++t)
-        for (int64_t c = t; c < chunks; c += T)
+    for (int t = 0; t < T; ++t) {
+        float lane[2] = {0.0f, 0.0f};
+        for (int l = 0; l < 2; ++l) {
+            int64_t c = (int64_t)(t / 16) * 32 + 16 * l + t % 16;
+            if (c >= chunks) continue;
             for (int j = 0; j < 16; ++j) {
                 float v = bf16_to_f32(xr[c * 16 + j]);
-                part[t] = part[t] + v * v;
+                lane[l] = lane[l] + v * v;
             }
+        }
+        part[t] = lane[0] + lane[1];
+    }
     float ss = block_tree_sum(part, T);
     free(part);
     float inv = 1.0f / sqrtf(ss / (float)K + eps);

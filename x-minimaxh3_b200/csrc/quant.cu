@@ -2,8 +2,10 @@
 //
 // Persistent CTAs of T threads (a multiple of 32, at most 512) walk the token
 // rows (the next row is loaded while the current one is processed); thread t
-// owns the 16-column chunks c = t, t+T, ... of the row, so every global access
-// is a 32-byte vector load or a 16-byte vector store.  Variants (template):
+// owns two 16-column chunks of the row, chunk t % 16 of the 256-column groups
+// 2p and 2p + 1 (p = t / 16), held as the two lanes of packed float pairs, so
+// every global access is a 32-byte vector load or a 16-byte vector store and the
+// arithmetic runs on packed fp32 pairs.  Variants (template):
 //   * plain row quantization        (comfy_kitchen int8_linear.cu:158-200)
 //   * ConvRot-256 + row quantization (int8_linear.cu:943-1030), with the
 //     optional input activation gelu_tanh / swiglu applied on load
@@ -21,73 +23,7 @@ namespace h3b {
 enum QuantMode : int { kPlain = 0, kConvRot = 1 };
 
 
-constexpr int kMaxIters = 2;  // chunks per thread; K <= 2 * 512 * 16 = 16384
 
-// One radix-4 butterfly of the regular H4 matrix, outputs in the reference's
-// operation order (int8_linear.cu:217-250): y0 = ((x0+x1)+x2)-x3,
-// y1 = ((x0+x1)-x2)+x3, y2 = ((x0-x1)+x2)+x3, y3 = ((-x0+x1)+x2)+x3, times 1/2.
-// x0+x1 and x0-x1 are shared; (-x0+x1)+x2 == x2-(x0-x1) exactly.
-__device__ __forceinline__ void h4_stage(const float* x, int s, float* y, int base) {
-  const float x0 = x[base], x1 = x[base + s], x2 = x[base + 2 * s], x3 = x[base + 3 * s];
-  const float s01 = __fadd_rn(x0, x1), d01 = __fsub_rn(x0, x1);
-  y[base] = __fmul_rn(0.5f, __fsub_rn(__fadd_rn(s01, x2), x3));
-  y[base + s] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(s01, x2), x3));
-  y[base + 2 * s] = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(d01, x2), x3));
-  y[base + 3 * s] = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(x2, d01), x3));
-}
-
-// Two radix-4 stages (stride 1 then 4) over 16 values held by one thread.
-__device__ __forceinline__ void fht16(float (&v)[16]) {
-  float t[16];
-#pragma unroll
-  for (int b0 = 0; b0 < 16; b0 += 4) h4_stage(v, 1, t, b0);
-#pragma unroll
-  for (int b0 = 0; b0 < 4; ++b0) h4_stage(t, 4, v, b0);
-}
-
-// exp(x) for x in [-20, 0], the argument range of the GELU's tanh: the IEEE
-// operations of h3b_expf on that range without its range branches.  rint(x log2 e)
-// is taken by adding and subtracting 1.5 * 2^23 (round half to even, as rintf),
-// the integer exponent comes from that sum's low bits, and one power-of-two
-// scaling replaces the two half scalings (equal, since every product stays
-// normal for n >= -29).  Matches h3b_expf bit for bit on every float of [-20, 0].
-__device__ __forceinline__ float expf_neg20(float x) {
-  const float kLog2e = 1.44269502162933349609375f;
-  const float kLn2Hi = 0.693145751953125f;
-  const float kLn2Lo = 1.428606765330187045e-06f;
-  const float t = __fadd_rn(__fmul_rn(x, kLog2e), 12582912.0f);
-  const float n = __fsub_rn(t, 12582912.0f);
-  float r = fmaf(-n, kLn2Hi, x);
-  r = fmaf(-n, kLn2Lo, r);
-  float p = 1.0f / 5040.0f;
-  p = fmaf(p, r, 1.0f / 720.0f);
-  p = fmaf(p, r, 1.0f / 120.0f);
-  p = fmaf(p, r, 1.0f / 24.0f);
-  p = fmaf(p, r, 1.0f / 6.0f);
-  p = fmaf(p, r, 0.5f);
-  p = fmaf(p, r, 1.0f);
-  p = fmaf(p, r, 1.0f);
-  const int ni = (int)(__float_as_uint(t) - 0x4B400000u);
-  return __fmul_rn(p, __uint_as_float((uint32_t)(ni + 127) << 23));
-}
-// h3b_tanhf without branches: (1 - e) / (1 + e) correctly rounded by Markstein's
-// final step from RN(1 / (1 + e)) (equal to IEEE division for every e in
-// [2e-9, 1], the range exp(-2|x|) takes for |x| < 10); |x| >= 10 gives +-1.
-__device__ __forceinline__ float tanh_gelu(float x) {
-  const float a = fabsf(x);
-  const float e = expf_neg20(__fmul_rn(-2.0f, a));
-  const float num = __fsub_rn(1.0f, e), den = __fadd_rn(1.0f, e);
-  float t = div_rn_by(num, den, __frcp_rn(den));
-  t = x < 0.0f ? -t : t;
-  return a >= 10.0f ? (x > 0.0f ? 1.0f : -1.0f) : t;
-}
-__device__ __forceinline__ float gelu_tanh(float v) {
-  const float kBeta = 0.7978845608028654f;
-  const float kKappa = 0.044715f;
-  float cube = __fmul_rn(__fmul_rn(__fmul_rn(kKappa, v), v), v);
-  float inner = __fmul_rn(kBeta, __fadd_rn(v, cube));
-  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanh_gelu(inner)));
-}
 // int8 code of a scaled value s: clamp to [-128, 127], round half to even by
 // adding 1.5 * 2^23, and take the low byte of the sum's bits -- the code of
 // rintf + clamp + (int) (clamping first cannot change the rounded result).
@@ -97,17 +33,6 @@ __device__ __forceinline__ uint32_t code_byte(float s) {
 }
 __device__ __forceinline__ float swiglu(float gate, float up) {
   return __fmul_rn(__fdiv_rn(gate, __fadd_rn(1.0f, h3b_expf(-gate))), up);
-}
-
-__device__ __forceinline__ void load16_bf16(const uint16_t* p, float (&v)[16]) {
-  const uint4 a = *reinterpret_cast<const uint4*>(p);
-  const uint4 b = *reinterpret_cast<const uint4*>(p + 8);
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
 }
 
 // Warp shfl_down tree then the same tree over the (zero padded) warp sums:
@@ -148,177 +73,287 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[32];
 }
 
+// ---------------------------------------------------------------- packed pairs
+// Every thread owns chunk i of two neighbouring 256-column groups (chunks
+// 32p + i and 32p + 16 + i, p = thread / 16, i = thread % 16) and keeps the two
+// as the lanes of float2 values, so the per-element arithmetic runs as packed
+// FFMA2 / FADD2 / FMUL2 -- IEEE round-to-nearest per lane, the same bits as the
+// scalar operations -- and both lanes take the same place in their groups'
+// 16 x 16 transform arrays.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+// a - b with one rounding: b * -1 is exact, so the fused product-add rounds a - b
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
+// both lanes rounded to bf16 (cvt.rn.bf16x2.f32) and widened back
+__device__ __forceinline__ float2 bf16r2(float2 v) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v.y), "f"(v.x));
+  return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
+}
+__device__ __forceinline__ float2 div2_rn_by(float2 a, float2 b, float2 rb) {
+  const float2 q = mul2(a, rb);
+  const float2 r = fma2(q, make_float2(-b.x, -b.y), a);
+  return fma2(r, rb, q);
+}
+
+// One radix-4 butterfly of the regular H4 matrix on both lanes, outputs in the
+// reference's operation order (int8_linear.cu:217-250): y0 = ((x0+x1)+x2)-x3,
+// y1 = ((x0+x1)-x2)+x3, y2 = ((x0-x1)+x2)+x3, y3 = ((-x0+x1)+x2)+x3, times 1/2.
+// x0+x1 and x0-x1 are shared; (-x0+x1)+x2 == x2-(x0-x1) exactly.
+__device__ __forceinline__ void h4_stage2(const float2* x, int s, float2* y, int base) {
+  const float2 h = splat2(0.5f);
+  const float2 x0 = x[base], x1 = x[base + s], x2 = x[base + 2 * s], x3 = x[base + 3 * s];
+  const float2 s01 = add2(x0, x1), d01 = sub2(x0, x1);
+  y[base] = mul2(h, sub2(add2(s01, x2), x3));
+  y[base + s] = mul2(h, add2(sub2(s01, x2), x3));
+  y[base + 2 * s] = mul2(h, add2(add2(d01, x2), x3));
+  y[base + 3 * s] = mul2(h, add2(sub2(x2, d01), x3));
+}
+// Two radix-4 stages (stride 1 then 4) over the 16 values of each lane.
+__device__ __forceinline__ void fht16x2(float2 (&v)[16]) {
+  float2 t[16];
+#pragma unroll
+  for (int b0 = 0; b0 < 16; b0 += 4) h4_stage2(v, 1, t, b0);
+#pragma unroll
+  for (int b0 = 0; b0 < 4; ++b0) h4_stage2(t, 4, v, b0);
+}
+
+// exp(x) for x in [-20, 0], the argument range of the GELU's tanh, on both
+// lanes: the IEEE operations of h3b_expf on that range without its range
+// branches.  rint(x log2 e) is taken by adding and subtracting 1.5 * 2^23 (round
+// half to even, as rintf), the integer exponent comes from that sum's low bits,
+// and one power-of-two scaling replaces the two half scalings (equal, since every
+// product stays normal for n >= -29).  Matches h3b_expf bit for bit on every
+// float of [-20, 0].
+__device__ __forceinline__ float2 expf_neg20x2(float2 x) {
+  const float kLog2e = 1.44269502162933349609375f;
+  const float kLn2Hi = 0.693145751953125f;
+  const float kLn2Lo = 1.428606765330187045e-06f;
+  const float2 t = add2(mul2(x, splat2(kLog2e)), splat2(12582912.0f));
+  const float2 n = sub2(t, splat2(12582912.0f));
+  float2 r = fma2(n, splat2(-kLn2Hi), x);
+  r = fma2(n, splat2(-kLn2Lo), r);
+  float2 p = splat2(1.0f / 5040.0f);
+  p = fma2(p, r, splat2(1.0f / 720.0f));
+  p = fma2(p, r, splat2(1.0f / 120.0f));
+  p = fma2(p, r, splat2(1.0f / 24.0f));
+  p = fma2(p, r, splat2(1.0f / 6.0f));
+  p = fma2(p, r, splat2(0.5f));
+  p = fma2(p, r, splat2(1.0f));
+  p = fma2(p, r, splat2(1.0f));
+  const int nx = (int)(__float_as_uint(t.x) - 0x4B400000u), ny = (int)(__float_as_uint(t.y) - 0x4B400000u);
+  return mul2(p, make_float2(__uint_as_float((uint32_t)(nx + 127) << 23), __uint_as_float((uint32_t)(ny + 127) << 23)));
+}
+// RN(1 / d) for d in [1, 2]: the approximate reciprocal refined by one Newton
+// step, y + y (1 - d y).  Checked against the IEEE reciprocal (__frcp_rn) on
+// every float of [1, 2] on B200: identical bits.
+__device__ __forceinline__ float2 rcp2_1to2(float2 d) {
+  float yx, yy;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yx) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yy) : "f"(d.y));
+  const float2 y = make_float2(yx, yy);
+  return fma2(fma2(make_float2(-d.x, -d.y), y, splat2(1.0f)), y, y);
+}
+// GELU (tanh form) on both lanes.  tanh(x) = sign(x) (1 - e) / (1 + e), e =
+// exp(-2|x|): the quotient is correctly rounded by Markstein's final step from
+// RN(1 / (1 + e)) (equal to IEEE division for every e in [2e-9, 1], the range
+// exp(-2|x|) takes for |x| < 10).  The exponent is clamped at -20, so |x| >= 10
+// gives e = exp(-20), 1 - e and 1 + e both round to 1 and tanh = +-1 exactly; the
+// sign is the sign bit of x (t >= 0; a -0 only ever reaches 1 + t).
+__device__ __forceinline__ float2 gelu_tanh2(float2 v) {
+  const float kBeta = 0.7978845608028654f;
+  const float kKappa = 0.044715f;
+  const float2 cube = mul2(mul2(mul2(splat2(kKappa), v), v), v);
+  const float2 x = mul2(splat2(kBeta), add2(v, cube));
+  const float2 m2a = mul2(splat2(-2.0f), make_float2(fabsf(x.x), fabsf(x.y)));
+  const float2 e = expf_neg20x2(make_float2(fmaxf(m2a.x, -20.0f), fmaxf(m2a.y, -20.0f)));
+  const float2 num = sub2(splat2(1.0f), e), den = add2(splat2(1.0f), e);
+  float2 t = div2_rn_by(num, den, rcp2_1to2(den));
+  t.x = __uint_as_float(__float_as_uint(t.x) | (__float_as_uint(x.x) & 0x80000000u));
+  t.y = __uint_as_float(__float_as_uint(t.y) | (__float_as_uint(x.y) & 0x80000000u));
+  return mul2(mul2(splat2(0.5f), v), add2(splat2(1.0f), t));
+}
+
+__device__ __forceinline__ uint4 ldg4(const uint16_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// 16 bf16 of chunk-lane x (words wx) and lane y (words wy) -> 16 float2
+__device__ __forceinline__ void unpack16x2(const uint4 (&wx)[2], const uint4 (&wy)[2], float2 (&v)[16]) {
+  const uint32_t qx[8] = {wx[0].x, wx[0].y, wx[0].z, wx[0].w, wx[1].x, wx[1].y, wx[1].z, wx[1].w};
+  const uint32_t qy[8] = {wy[0].x, wy[0].y, wy[0].z, wy[0].w, wy[1].x, wy[1].y, wy[1].z, wy[1].w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = make_float2(__uint_as_float(qx[i] << 16), __uint_as_float(qy[i] << 16));
+    v[2 * i + 1] = make_float2(__uint_as_float(qx[i] & 0xffff0000u), __uint_as_float(qy[i] & 0xffff0000u));
+  }
+}
+__device__ __forceinline__ void load_pair(const uint16_t* base, int cx, int cy, bool lx, bool ly, uint4 (&wx)[2],
+                                          uint4 (&wy)[2]) {
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  wx[0] = lx ? ldg4(base + cx * 16) : z;
+  wx[1] = lx ? ldg4(base + cx * 16 + 8) : z;
+  wy[0] = ly ? ldg4(base + cy * 16) : z;
+  wy[1] = ly ? ldg4(base + cy * 16 + 8) : z;
+}
+
 // raw bf16 chunks of one row owned by this thread (prefetched one row ahead)
 struct RowRegs {
-  uint4 x[kMaxIters][2];
-  uint4 u[kMaxIters][2];  // the `up` half of a swiglu row
+  uint4 x[2][2];  // [lane][half]
+  uint4 u[2][2];  // the `up` half of a swiglu row
 };
 
 template <int ACT>
-__device__ __forceinline__ void load_row(const QuantArgs& a, int64_t row, int t, int T, int chunks, RowRegs& r) {
+__device__ __forceinline__ void load_row(const QuantArgs& a, int64_t row, int cx, int cy, bool lx, bool ly,
+                                         RowRegs& r) {
   const uint16_t* xr = a.x + row * a.x_stride;
-#pragma unroll
-  for (int i = 0; i < kMaxIters; ++i) {
-    const int c = t + i * T;
-    if (c < chunks) {
-      const uint4* p = reinterpret_cast<const uint4*>(xr + c * 16);
-      r.x[i][0] = __ldg(p);
-      r.x[i][1] = __ldg(p + 1);
-      if (ACT == 2) {
-        const uint4* pu = reinterpret_cast<const uint4*>(xr + a.K + c * 16);
-        r.u[i][0] = __ldg(pu);
-        r.u[i][1] = __ldg(pu + 1);
-      }
-    }
-  }
+  load_pair(xr, cx, cy, lx, ly, r.x[0], r.x[1]);
+  if (ACT == 2) load_pair(xr + a.K, cx, cy, lx, ly, r.u[0], r.u[1]);
 }
 
-__device__ __forceinline__ void unpack16(const uint4 (&w)[2], float (&v)[16]) {
-  const uint32_t q[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = __uint_as_float(q[i] << 16);
-    v[2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
-  }
+// int8 codes of both lanes: the scalar code_byte(bf16(bf16(v) / st)) lane by lane
+__device__ __forceinline__ void codes2(float2 v, float2 st2, float2 rst2, uint32_t& bx, uint32_t& by) {
+  const float2 d = bf16r2(div2_rn_by(bf16r2(v), st2, rst2));
+  bx = code_byte(d.x);
+  by = code_byte(d.y);
 }
 
 // Persistent: CTA b handles rows b, b + gridDim.x, ...; the next row's loads are
 // issued before the current row is processed.
 template <int MODE, int ACT, bool RMS>
 __global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t rows) {
-  extern __shared__ float tile[];       // (T/16) groups x 16 x 17 floats
+  extern __shared__ float2 tile2[];     // (T/16) groups x 16 x 17 float2
   __shared__ float red[33];
-  const int T = blockDim.x, t = threadIdx.x;
+  const int t = threadIdx.x;
   const int K = a.K, chunks = K >> 4;
-  float* my_tile = tile + (t >> 4) * (16 * 17);
-  const int a_idx = t & 15;  // row of the 16x16 group array owned for loads / stores
+  const int idx = t & 15;                    // place in the group's 16 x 16 array
+  const int cx = (t >> 4) * 32 + idx, cy = cx + 16;
+  const bool lx = cx < chunks, ly = cy < chunks;
+  float2* my_tile = tile2 + (t >> 4) * (16 * 17);
 
   RowRegs nxt;
   int64_t row = blockIdx.x;
-  if (row < rows) load_row<ACT>(a, row, t, T, chunks, nxt);
+  if (row < rows) load_row<ACT>(a, row, cx, cy, lx, ly, nxt);
   for (; row < rows; row += gridDim.x) {
     const RowRegs cur = nxt;
-    if (row + gridDim.x < rows) load_row<ACT>(a, row + gridDim.x, t, T, chunks, nxt);
+    if (row + gridDim.x < rows) load_row<ACT>(a, row + gridDim.x, cx, cy, lx, ly, nxt);
 
-    float v[kMaxIters][16];
-    bool live[kMaxIters];
+    float2 v[16];
+    unpack16x2(cur.x[0], cur.x[1], v);
+    if (ACT == 2) {
+      float2 u[16];
+      unpack16x2(cur.u[0], cur.u[1], u);
 #pragma unroll
-    for (int i = 0; i < kMaxIters; ++i) {
-      live[i] = t + i * T < chunks;
-      if (live[i]) {
-        unpack16(cur.x[i], v[i]);
-        if (ACT == 2) {
-          float u[16];
-          unpack16(cur.u[i], u);
+      for (int j = 0; j < 16; ++j) v[j] = make_float2(swiglu(v[j].x, u[j].x), swiglu(v[j].y, u[j].y));
+    } else if (ACT == 1) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[i][j] = swiglu(v[i][j], u[j]);
-        } else if (ACT == 1) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[i][j] = gelu_tanh(v[i][j]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
-      }
+      for (int j = 0; j < 16; ++j) v[j] = gelu_tanh2(v[j]);
     }
+    // dead lanes hold zeros (loaded as zero, and every activation maps 0 to 0)
 
     if (RMS) {
-      float part = 0.0f;
+      // sum of squares: each lane in column order, then lane x + lane y, then the block tree
+      float2 part2 = splat2(0.0f);
 #pragma unroll
-      for (int i = 0; i < kMaxIters; ++i)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) part = __fadd_rn(part, __fmul_rn(v[i][j], v[i][j]));
-      const float ss = block_tree_sum(part, red);
-      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+      for (int j = 0; j < 16; ++j) part2 = add2(part2, mul2(v[j], v[j]));
+      const float ss = block_tree_sum(__fadd_rn(part2.x, part2.y), red);
+      const float2 inv = splat2(__fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps))));
       const int r = a.seg_row ? a.seg_row[row] : 0;
-      const uint16_t* sc = a.scale_tab + (int64_t)r * K;
-      const uint16_t* sh = a.shift_tab + (int64_t)r * K;
+      const uint16_t* tabs[3] = {a.norm_w, a.scale_tab + (int64_t)r * K, a.shift_tab + (int64_t)r * K};
 #pragma unroll
-      for (int i = 0; i < kMaxIters; ++i) {
-        if (!live[i]) continue;
-        const int c0 = (t + i * T) * 16;
-        float w[16], s1[16], s2[16];
-        load16_bf16(a.norm_w + c0, w);
-        load16_bf16(sc + c0, s1);
-        load16_bf16(sh + c0, s2);
+      for (int h = 0; h < 2; ++h) {  // 8 columns of each lane at a time
+        float2 w[3][8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float n = bf16r(__fmul_rn(__fmul_rn(v[i][j], inv), w[j]));
-          n = bf16r(__fmul_rn(n, bf16r(__fadd_rn(1.0f, s1[j]))));
-          v[i][j] = bf16r(__fadd_rn(n, s2[j]));
+        for (int k = 0; k < 3; ++k) {
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+          const uint4 wx = lx ? ldg4(tabs[k] + cx * 16 + 8 * h) : z;
+          const uint4 wy = ly ? ldg4(tabs[k] + cy * 16 + 8 * h) : z;
+          const uint32_t qx[4] = {wx.x, wx.y, wx.z, wx.w}, qy[4] = {wy.x, wy.y, wy.z, wy.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            w[k][2 * i] = make_float2(__uint_as_float(qx[i] << 16), __uint_as_float(qy[i] << 16));
+            w[k][2 * i + 1] = make_float2(__uint_as_float(qx[i] & 0xffff0000u), __uint_as_float(qy[i] & 0xffff0000u));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float2 n = bf16r2(mul2(mul2(v[8 * h + j], inv), w[0][j]));
+          n = bf16r2(mul2(n, bf16r2(add2(splat2(1.0f), w[1][j]))));
+          v[8 * h + j] = bf16r2(add2(n, w[2][j]));
         }
       }
+      // dead lanes: weight, scale and shift load as 0, so v stays 0
     }
 
     if (MODE == kConvRot) {
+      fht16x2(v);
+      __syncthreads();
 #pragma unroll
-      for (int i = 0; i < kMaxIters; ++i) {
-        if (i * T >= chunks) break;  // uniform across the block
-        fht16(v[i]);
-        __syncthreads();
+      for (int b = 0; b < 16; ++b) my_tile[idx * 17 + b] = v[b];
+      __syncthreads();
+      // the thread now holds column idx of both groups' arrays
 #pragma unroll
-        for (int b = 0; b < 16; ++b) my_tile[a_idx * 17 + b] = v[i][b];
-        __syncthreads();
-        // thread now takes column b = a_idx of its group
-#pragma unroll
-        for (int r = 0; r < 16; ++r) v[i][r] = my_tile[r * 17 + a_idx];
-        fht16(v[i]);
-      }
+      for (int r = 0; r < 16; ++r) v[r] = my_tile[r * 17 + idx];
+      fht16x2(v);
     }
 
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kMaxIters; ++i)
-      if (live[i])
-#pragma unroll
-        for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
     amax = block_max(amax, red);
     const float scale = fmaxf(__fmul_rn(fminf(amax, 3.38953139e38f), 1.0f / 127.0f), 1.0e-30f);
     const float st = bf16r(scale);
-    const float rst = __fdiv_rn(1.0f, st);
+    const float2 st2 = splat2(st), rst2 = splat2(__fdiv_rn(1.0f, st));
     if (t == 0) a.scales[row] = scale;
 
+    uint32_t px[4], py[4];
+#pragma unroll
+    for (int w4 = 0; w4 < 4; ++w4) {
+      uint32_t wxv = 0, wyv = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t bx, by;
+        codes2(v[4 * w4 + j], st2, rst2, bx, by);
+        wxv |= bx << (8 * j);
+        wyv |= by << (8 * j);
+      }
+      px[w4] = wxv;
+      py[w4] = wyv;
+    }
     int8_t* qr = a.q + row * (int64_t)K;
+    if (MODE == kConvRot) {
+      // codes are held by column; transpose both groups back through shared memory
+      uint8_t* bt = reinterpret_cast<uint8_t*>(my_tile);
+      __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kMaxIters; ++i) {
-      if (i * T >= chunks) break;
-      uint32_t packed[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          word |= code_byte(bf16r(div_rn_by(bf16r(v[i][4 * w + j]), st, rst))) << (8 * j);
-        }
-        packed[w] = word;
+      for (int r = 0; r < 16; ++r) {
+        bt[r * 16 + idx] = (uint8_t)(px[r >> 2] >> (8 * (r & 3)));
+        bt[256 + r * 16 + idx] = (uint8_t)(py[r >> 2] >> (8 * (r & 3)));
       }
-      if (MODE == kConvRot) {
-        // codes are held by column; transpose back through shared memory
-        uint8_t* bt = reinterpret_cast<uint8_t*>(my_tile);
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < 16; ++r) bt[r * 16 + a_idx] = (uint8_t)(packed[r >> 2] >> (8 * (r & 3)));
-        __syncthreads();
-        const uint4 row16 = *reinterpret_cast<const uint4*>(bt + a_idx * 16);
-        if (live[i]) *reinterpret_cast<uint4*>(qr + (t + i * T) * 16) = row16;
-      } else if (live[i]) {
-        *reinterpret_cast<uint4*>(qr + (t + i * T) * 16) =
-            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      }
+      __syncthreads();
+      const uint4 rx = *reinterpret_cast<const uint4*>(bt + idx * 16);
+      const uint4 ry = *reinterpret_cast<const uint4*>(bt + 256 + idx * 16);
+      if (lx) *reinterpret_cast<uint4*>(qr + cx * 16) = rx;
+      if (ly) *reinterpret_cast<uint4*>(qr + cy * 16) = ry;
+    } else {
+      if (lx) *reinterpret_cast<uint4*>(qr + cx * 16) = make_uint4(px[0], px[1], px[2], px[3]);
+      if (ly) *reinterpret_cast<uint4*>(qr + cy * 16) = make_uint4(py[0], py[1], py[2], py[3]);
     }
   }
 }
 
+// Threads per row: 16 per pair of 256-column groups (chunk pairs), rounded up to
+// a warp multiple; K <= 16384 gives at most 512.
 int quant_threads_for(int K) {
-  int chunks = K / 16;
-  int T = ((chunks + 31) / 32) * 32;
-  return T > 512 ? 512 : T;
+  const int chunks = K / 16;
+  const int groups = (chunks + 15) / 16;
+  const int T = ((groups + 1) / 2) * 16;
+  return ((T + 31) / 32) * 32;
 }
 
 template <int MODE, int ACT, bool RMS>
 static cudaError_t launch_q(const QuantArgs& a, int64_t rows, cudaStream_t s) {
   const int T = quant_threads_for(a.K);
-  const size_t smem = (size_t)(T / 16) * 16 * 17 * sizeof(float);
+  const size_t smem = (size_t)(T / 16) * 16 * 17 * sizeof(float2);
   auto k = quant_rows_kernel<MODE, ACT, RMS>;
   if (smem > 48 * 1024) {
     cudaError_t e0 = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
