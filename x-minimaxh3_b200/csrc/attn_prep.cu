@@ -224,8 +224,10 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
       for (int i = 0; i < 4; ++i) {
         float t = div_rn_by(v[i], sc, rsc);
         t = __fadd_rn(t, t >= 0.0f ? 0.5f : -0.5f);
-        float tr = fminf(127.0f, fmaxf(-127.0f, truncf(t)));
-        word |= ((uint32_t)(int)tr & 0xffu) << (8 * i);
+        // trunc, clamp to [-127, 127], to int: clamping first gives the same code
+        // (also for NaN, which both orders send to -127) with one conversion
+        const int code = __float2int_rz(fminf(127.0f, fmaxf(-127.0f, t)));
+        word |= ((uint32_t)code & 0xffu) << (8 * i);
       }
     }
     *reinterpret_cast<uint32_t*>(a.q + ((int64_t)h * a.Lpad + r0 + r) * kD + 4 * lane) = word;
@@ -261,6 +263,13 @@ __device__ __forceinline__ void load4_bf16(const uint16_t* p, bool vec, float (&
   }
 }
 
+// two floats rounded to bf16 (cvt.rn.bf16x2.f32): lo in bits 0..15, hi in 16..31
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(QkRopeArgs a) {
   const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -293,24 +302,28 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(QkRopeArgs a) {
                                            __fmul_rn(v[2], v[2])),
                                  __fmul_rn(v[3], v[3]));
       const float ss = warp_butterfly_sum(sq);
-      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
-      float n[4];
+      // ss / 128 is a scaling by 2^-7: the product rounds the same value the division does
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 0.0078125f), a.eps)));
+      // normalized values, rounded to bf16 two at a time; kept as packed bf16 pairs
+      const uint32_t n01 = bf16x2_bits(__fmul_rn(__fmul_rn(v[0], inv), wv[0]), __fmul_rn(__fmul_rn(v[1], inv), wv[1]));
+      const uint32_t n23 = bf16x2_bits(__fmul_rn(__fmul_rn(v[2], inv), wv[2]), __fmul_rn(__fmul_rn(v[3], inv), wv[3]));
+      // the rotation partner of each value, two per shuffle
+      const uint32_t p01 = __shfl_sync(0xffffffffu, n01, rot ? src : lane);
+      const uint32_t p23 = __shfl_sync(0xffffffffu, n23, rot ? src : lane);
+      uint2 outw = make_uint2(n01, n23);
+      if (rot) {
+        const float n[4] = {__uint_as_float(n01 << 16), __uint_as_float(n01 & 0xffff0000u),
+                            __uint_as_float(n23 << 16), __uint_as_float(n23 & 0xffff0000u)};
+        const float pt[4] = {__uint_as_float(p01 << 16), __uint_as_float(p01 & 0xffff0000u),
+                             __uint_as_float(p23 << 16), __uint_as_float(p23 & 0xffff0000u)};
+        float o[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) n[i] = bf16r(__fmul_rn(__fmul_rn(v[i], inv), wv[i]));
-      float o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float partner = __shfl_sync(0xffffffffu, n[i], rot ? src : lane);
-        if (rot) {
-          o[i] = first ? bf16r(__fsub_rn(__fmul_rn(n[i], c[i]), __fmul_rn(partner, sn[i])))
-                       : bf16r(__fadd_rn(__fmul_rn(partner, sn[i]), __fmul_rn(n[i], c[i])));
-        } else {
-          o[i] = n[i];
-        }
+        for (int i = 0; i < 4; ++i)
+          o[i] = first ? __fsub_rn(__fmul_rn(n[i], c[i]), __fmul_rn(pt[i], sn[i]))
+                       : __fadd_rn(__fmul_rn(pt[i], sn[i]), __fmul_rn(n[i], c[i]));
+        outw = make_uint2(bf16x2_bits(o[0], o[1]), bf16x2_bits(o[2], o[3]));
       }
-      *reinterpret_cast<uint2*>(p) =
-          make_uint2((uint32_t)f32_to_bf16_bits(o[0]) | ((uint32_t)f32_to_bf16_bits(o[1]) << 16),
-                     (uint32_t)f32_to_bf16_bits(o[2]) | ((uint32_t)f32_to_bf16_bits(o[3]) << 16));
+      *reinterpret_cast<uint2*>(p) = outw;
     }
   }
 }

@@ -12,6 +12,9 @@ Cases:
     quant_convrot              h3b_quantize_int8_rowwise_convrot, 65,536 x 4,096
     quant_gelu                 the same with the tanh-GELU input activation, 16,384 x 16,384
     rms_adaln                  h3b_rms_adaln_quantize_int8 (ConvRot), 65,536 x 4,096
+    pool_q                     h3b_pool_sim_quant on the queries, L = 65,536, 32 heads, 128-row blocks
+    mask                       h3b_block_mask (cdf 0.6 + first column + diagonal), L = 65,536, 32 heads
+    qk_rope                    h3b_qk_rmsnorm_rope on QKV rows [65,536, 3 x 4,096], rotary width 128
 """
 
 from __future__ import annotations
@@ -57,6 +60,22 @@ def _case(name: str, g: torch.Generator):
         sc = (0.1 * torch.randn(4096, device=dev, generator=g)).bfloat16()
         sh = (0.1 * torch.randn(4096, device=dev, generator=g)).bfloat16()
         return lambda: ops.rms_adaln_quantize_int8(x, w, sc, sh, None, 1e-5, 256)
+    if name in ("pool_q", "mask"):
+        L, H = 65536, 32
+        q, k = (torch.randn(L, H, 128, device=dev, generator=g).bfloat16() for _ in range(2))
+        if name == "pool_q":
+            return lambda: A.prepare_queries(q)
+        pq = A.prepare_queries(q)
+        pk, _ = A.prepare_keys(k)
+        cfg = A.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True)
+        return lambda: A.block_mask(pq, pk, cfg)
+    if name == "qk_rope":
+        L, H = 65536, 32
+        qkv = torch.randn(L, 3 * H * 128, device=dev, generator=g).bfloat16()
+        w = (1 + 0.05 * torch.randn(128, device=dev, generator=g)).bfloat16()
+        ang = torch.rand(L, 64, device=dev, generator=g) * 6.0
+        cos, sin = ang.cos().bfloat16(), ang.sin().bfloat16()
+        return lambda: ops.qk_rmsnorm_rope_(qkv, H, 0, H * 128, w, w, cos, sin, 1e-6)
     raise SystemExit(f"unknown case {name!r}")
 
 
