@@ -184,3 +184,17 @@ def test_oracle_layers_against_engine_layer_outputs(ckpt, golden):
             sx = q.reshape(q.shape[0], -1, group).astype(np.int64).sum(-1) * s.reshape(-1, 1)
             out = out + sx @ t["weight_correction"].float().numpy()
         assert rel_l2(out, O.bf16_bits_to_f32(golden[f"layer_{tag}_out"])) < 2e-2, tag
+
+
+def test_chunk_segments_restrict_and_shift():
+    from h3b.block import _chunk_segments, _runs
+    segs = ((0, 300, 0), (300, 700, 4), (700, 1024, 5))
+    assert _chunk_segments(None, 0, 10) is None
+    assert _chunk_segments(segs, 0, 100) == ((0, 100, 0),)
+    assert _chunk_segments(segs, 100, 517) == ((0, 200, 0), (200, 417, 4))
+    assert _chunk_segments(segs, 517, 1024) == ((0, 183, 4), (183, 507, 5))
+    for r0, r1 in ((0, 100), (100, 517), (517, 1000), (1000, 1024)):
+        runs = _runs(_chunk_segments(segs, r0, r1), r1 - r0, 6)
+        assert runs[0][0] == 0 and runs[-1][1] == r1 - r0
+    with pytest.raises(ValueError):
+        _runs(((0, 5, 0), (6, 10, 1)), 10, 6)

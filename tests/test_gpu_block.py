@@ -122,3 +122,23 @@ def test_host_pipeline_matches_sequential_forwards(blockmod):
     for k in range(steps):
         ref = blk.forward(xs[k].cuda(), ts[k].cuda(), rope).cpu()
         assert torch.equal(outs[k], ref), k
+
+
+def test_chunked_forward_matches_single_chunk(blockmod):
+    """The row-local phases run chunk by chunk give the bits of the whole-row run,
+    with AdaLN segments that cross the chunk boundaries."""
+    B = blockmod
+    cfg = B.BlockConfig(hidden=1024, heads=8, ffn=4096, t_dim=256)
+    blk = B.DiTBlockB200(cfg, device="cuda", seed=7)
+    L = 1024
+    g = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(L, cfg.hidden, generator=g, device="cuda").to(torch.bfloat16)
+    t = torch.randn(3, cfg.t_dim, generator=g, device="cuda").to(torch.bfloat16)
+    rope = B.rope_tables((4, 16, 16), cfg.rope_splits, device="cuda")
+    segments = ((0, 300, 0), (300, 700, 1), (700, 1024, 2))
+    whole = blk.forward(x.clone(), t, rope, segments=segments)
+    seen = []
+    chunked = blk.forward(x.clone(), t, rope, segments=segments, chunks=[0, 100, 517, 1000, 1024],
+                          rows_ready=lambda i: seen.append(("in", i)), rows_done=lambda i: seen.append(("out", i)))
+    assert torch.equal(whole, chunked)
+    assert seen == [("in", 0), ("in", 1), ("in", 2), ("in", 3), ("out", 0), ("out", 1), ("out", 2), ("out", 3)]

@@ -84,6 +84,18 @@ def _runs(segments, rows: int, table_rows: int):
     return runs
 
 
+def _chunk_segments(segments, r0: int, r1: int):
+    """AdaLN runs restricted to rows [r0, r1), in chunk-relative rows (None stays None)."""
+    if segments is None:
+        return None
+    out = []
+    for start, stop, row in segments:
+        a, b = max(int(start), r0), min(int(stop), r1)
+        if a < b:
+            out.append((a - r0, b - r0, int(row)))
+    return tuple(out)
+
+
 def rope_tables_from_frequencies(frequencies: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """(cos, sin) bf16 [L, rot/2] tables from the engine's RoPE input: split-half angles
     [L, rot] (model/layers.py:51-57) or the packed rotation table [1, L, 1, rot/2, 2, 2]
@@ -217,32 +229,55 @@ class DiTBlockB200:
             lin.gated_residual_(x[start:stop], gate[row], q[start:stop], s[start:stop])
 
     def forward(self, x: torch.Tensor, t: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor],
-                segments=None) -> torch.Tensor:
+                segments=None, *, chunks=None, rows_ready=None, rows_done=None) -> torch.Tensor:
         """x: bf16 [L_local, hidden] (updated in place and returned); rope: tables for these
         tokens; segments: AdaLN runs ((start, stop, row), ...) over x's rows, or None for
-        modulation row 0 everywhere (model/layers.py:916-960)."""
+        modulation row 0 everywhere (model/layers.py:916-960).
+
+        chunks: row boundaries [0, b1, ..., L_local] for the row-local phases (RMSNorm +
+        AdaLN + QKV + q/k RoPE before the attention; RMSNorm + AdaLN + MLP + gated residual
+        after it), which then run chunk by chunk.  rows_ready(i) is called before chunk i's
+        rows are first read, rows_done(i) once its final values are enqueued; a host pipeline
+        uses them to overlap row copies with the neighbouring chunks' work.  Every operation
+        of these phases is row-local, so the result does not depend on the chunking."""
         cfg = self.cfg
         mod = self.modulation(t)
         shift_a, scale_a, gate_a, shift_m, scale_m, gate_m = mod.unbind(1)
-        runs = _runs(segments, x.shape[0], mod.shape[0])
-        xq, xs = ops.rms_adaln_quantize_int8(x, self.norm1, scale_a, shift_a, segments, cfg.eps,
-                                             self.qkv.convrot_group_size)
-        qkv = self.qkv.forward_prequantized(xq, xs)
-        W = cfg.heads * cfg.head_dim
-        ops.qk_rmsnorm_rope_(qkv, cfg.heads, 0, W, self.q_norm, self.k_norm, rope[0], rope[1], cfg.qk_eps)
         Lp = x.shape[0]
+        runs = _runs(segments, Lp, mod.shape[0])
+        bounds = [0, Lp] if chunks is None else [int(b) for b in chunks]
+        if bounds[0] != 0 or bounds[-1] != Lp or any(b1 <= b0 for b0, b1 in zip(bounds, bounds[1:])):
+            raise ValueError("chunks must be increasing row boundaries from 0 to the row count")
+        W = cfg.heads * cfg.head_dim
+        qkv = torch.empty((Lp, 3 * W), device=x.device, dtype=torch.bfloat16)
+        for i, (r0, r1) in enumerate(zip(bounds, bounds[1:])):
+            if rows_ready is not None:
+                rows_ready(i)
+            seg_i = _chunk_segments(segments, r0, r1)
+            xq, xs = ops.rms_adaln_quantize_int8(x[r0:r1], self.norm1, scale_a, shift_a, seg_i, cfg.eps,
+                                                 self.qkv.convrot_group_size)
+            self.qkv.forward_prequantized(xq, xs, out=qkv[r0:r1])
+            ops.qk_rmsnorm_rope_(qkv[r0:r1], cfg.heads, 0, W, self.q_norm, self.k_norm, rope[0][r0:r1],
+                                 rope[1][r0:r1], cfg.qk_eps)
         if self.world > 1:
             o = self.attention(P.tokens_to_heads(qkv, cfg.heads, cfg.head_dim, self.group))
             o2 = P.heads_to_tokens(o.view(o.shape[0], -1), Lp, self.group)
         else:
             o2 = self.attention(qkv).view(Lp, W)
+        del qkv
         oq, os_ = self.out.quantize(o2)
         self._gated(self.out, x, gate_a, oq, os_, runs)
-        xq, xs = ops.rms_adaln_quantize_int8(x, self.norm2, scale_m, shift_m, segments, cfg.eps,
-                                             self.fc1.convrot_group_size)
-        h = self.fc1.forward_prequantized(xq, xs)
-        hq, hs = self.fc2.quantize(h, cfg.mlp_act)
-        self._gated(self.fc2, x, gate_m, hq, hs, runs)
+        del oq, os_, o2
+        for i, (r0, r1) in enumerate(zip(bounds, bounds[1:])):
+            seg_i = _chunk_segments(segments, r0, r1)
+            xq, xs = ops.rms_adaln_quantize_int8(x[r0:r1], self.norm2, scale_m, shift_m, seg_i, cfg.eps,
+                                                 self.fc1.convrot_group_size)
+            h = self.fc1.forward_prequantized(xq, xs)
+            hq, hs = self.fc2.quantize(h, cfg.mlp_act)
+            del h
+            self._gated(self.fc2, x[r0:r1], gate_m, hq, hs, _runs(seg_i, r1 - r0, mod.shape[0]))
+            if rows_done is not None:
+                rows_done(i)
         return x
 
     # ------------------------------------------------------------------ accounting
@@ -261,16 +296,21 @@ class HostPipeline:
     on their own streams: the host->device copy of step k + 1 and the
     device->host copy of step k - 1 overlap the block of step k (two device
     buffers; a buffer is refilled only after the result it held has been read
-    out).  All ordering is by CUDA events; nothing waits on the host.
+    out).  The first step's input arrives in `chunks` row chunks, and its block
+    starts on the first chunk while the rest copy; the last step's output leaves in
+    row chunks as the block finishes each one (the block's row-local phases run
+    chunk by chunk there).  All ordering is by CUDA events; nothing waits on the host.
     """
 
-    def __init__(self, block: DiTBlockB200, rope: tuple[torch.Tensor, torch.Tensor], tokens: int):
+    def __init__(self, block: DiTBlockB200, rope: tuple[torch.Tensor, torch.Tensor], tokens: int, chunks: int = 4):
         dev = block.device
         self.block, self.rope = block, rope
         self.x = [torch.empty((tokens, block.cfg.hidden), device=dev, dtype=torch.bfloat16) for _ in range(2)]
         self.t = [torch.empty((block.cfg.t_dim,), device=dev, dtype=torch.bfloat16) for _ in range(2)]
         self.s_in = torch.cuda.Stream(device=dev)
         self.s_out = torch.cuda.Stream(device=dev)
+        n = max(1, min(int(chunks), tokens))
+        self.bounds = [tokens * i // n for i in range(n + 1)]
 
     def run(self, xs_host: list[torch.Tensor], ts_host: list[torch.Tensor], outs_host: list[torch.Tensor]) -> None:
         """xs_host[k] / ts_host[k] (pinned, bf16) -> outs_host[k] (pinned, bf16), for every k.
@@ -285,19 +325,34 @@ class HostPipeline:
         comp = torch.cuda.current_stream(self.block.device)
         self.s_in.wait_stream(comp)
         self.s_out.wait_stream(comp)
-        loaded: list[torch.cuda.Event | None] = [None] * n
+        whole = [0, self.bounds[-1]]
+        loaded: list[list[torch.cuda.Event] | None] = [None] * n   # [t copied, row chunk 0, 1, ...]
         read_out: list[torch.cuda.Event | None] = [None, None]
+
+        def record(stream) -> torch.cuda.Event:
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            return ev
 
         def load(k: int) -> None:
             b = k % 2
+            bounds = self.bounds if k == 0 else whole
             with torch.cuda.stream(self.s_in):
                 if read_out[b] is not None:
                     self.s_in.wait_event(read_out[b])
-                self.x[b].copy_(xs_host[k], non_blocking=True)
                 self.t[b].copy_(ts_host[k], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(self.s_in)
-                loaded[k] = ev
+                evs = [record(self.s_in)]
+                for r0, r1 in zip(bounds, bounds[1:]):
+                    self.x[b][r0:r1].copy_(xs_host[k][r0:r1], non_blocking=True)
+                    evs.append(record(self.s_in))
+                loaded[k] = evs
+
+        def store(k: int, r0: int, r1: int) -> torch.cuda.Event:
+            done = record(comp)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(done)
+                outs_host[k][r0:r1].copy_(self.x[k % 2][r0:r1], non_blocking=True)
+                return record(self.s_out)
 
         if n:
             load(0)
@@ -305,16 +360,34 @@ class HostPipeline:
             if k + 1 < n:
                 load(k + 1)
             b = k % 2
-            comp.wait_event(loaded[k])
-            self.block.forward(self.x[b], self.t[b], self.rope)
-            done = torch.cuda.Event()
-            done.record(comp)
-            with torch.cuda.stream(self.s_out):
-                self.s_out.wait_event(done)
-                outs_host[k].copy_(self.x[b], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(self.s_out)
-                read_out[b] = ev
+            comp.wait_event(loaded[k][0])
+            first, last = k == 0, k == n - 1
+            if not (first or last):
+                comp.wait_event(loaded[k][1])
+                self.block.forward(self.x[b], self.t[b], self.rope)
+                read_out[b] = store(k, 0, whole[1])
+                continue
+            bounds = self.bounds
+            in_evs = loaded[k][1:]
+            outs: list[torch.cuda.Event] = []
+
+            def ready(i: int, k=k, in_evs=in_evs, bounds=bounds) -> None:
+                # chunk i of this step's rows: the copy that holds them has landed
+                if len(in_evs) == 1:
+                    if i == 0:
+                        comp.wait_event(in_evs[0])
+                else:
+                    comp.wait_event(in_evs[i])
+
+            def done(i: int, k=k, bounds=bounds) -> None:
+                if last:
+                    outs.append(store(k, bounds[i], bounds[i + 1]))
+
+            self.block.forward(self.x[b], self.t[b], self.rope, chunks=bounds, rows_ready=ready, rows_done=done)
+            if last:
+                read_out[b] = outs[-1]
+            else:
+                read_out[b] = store(k, 0, whole[1])
         comp.wait_stream(self.s_out)
 
 

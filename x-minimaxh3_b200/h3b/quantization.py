@@ -133,9 +133,10 @@ class _QuantLinear:
             raise ValueError("input_act is fused only into the ConvRot quantizer")
         return ops.quantize_int8_rowwise(x)
 
-    def forward_prequantized(self, xq: torch.Tensor, xs: torch.Tensor) -> torch.Tensor:
+    def forward_prequantized(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """bf16 [M, N] from quantized rows; `out` (bf16 rows with unit column stride) receives it when given."""
         w8, ws = self.int8_weight()
-        out = ops.int8_linear_prequantized(xq, xs, w8, ws, self.bias)
+        out = ops.int8_linear_prequantized(xq, xs, w8, ws, self.bias, out=out)
         self._correct_(out, xq, xs)
         return out
 
