@@ -29,6 +29,46 @@ __device__ __forceinline__ uint64_t fixed56(float p) {
   return __float2ull_rz(__fmul_rn(p, 72057594037927936.0f));
 }
 
+// Bins are scanned from the top (bin 255) down by the whole warp: lane l holds
+// bins 255 - 8l .. 248 - 8l.  The lanes' totals are prefix-summed across the warp
+// (lane 0 = top); the first lane whose running total crosses the bound then walks
+// its own 8 bins in order, which gives exactly what one thread walking all 256 bins
+// from the top would find.
+
+// First bin b (from the top) at which count(bins above b) + hist[b] >= need;
+// returns b and count(bins above b) in *above.  need <= the histogram's total.
+__device__ __forceinline__ int warp_find_count(const uint32_t* hist, uint32_t base, uint32_t need, int lane,
+                                               uint32_t* above) {
+  const int hi = 255 - 8 * lane;
+  uint32_t h[8], tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[i] = hist[hi - i];
+    tot += h[i];
+  }
+  uint32_t pre = tot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, pre, off);
+    if (lane >= off) pre += v;
+  }
+  const unsigned hit = __ballot_sync(0xffffffffu, base + pre >= need);
+  const int L = hit ? __ffs(hit) - 1 : 31;
+  int b = 0;
+  uint32_t cum = base + pre - tot;
+  if (lane == L) {
+    b = hi - 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (cum + h[i] >= need) { b = hi - i; break; }
+      cum += h[i];
+    }
+  }
+  b = __shfl_sync(0xffffffffu, b, L);
+  *above = __shfl_sync(0xffffffffu, cum, L);
+  return b;
+}
+
 // Threshold key T and how many of the keys equal to T to keep, so that exactly
 // `need` keys are kept (keys > T all kept).  hist: per-warp shared counters.
 __device__ void select_threshold(const uint16_t* keys, int Kb, int need, uint32_t* hist, int lane, int* T_out,
@@ -38,17 +78,8 @@ __device__ void select_threshold(const uint16_t* keys, int Kb, int need, uint32_
   __syncwarp();
   for (int j = lane; j < Kb; j += 32) atomicAdd(&hist[keys[j] >> 8], 1u);
   __syncwarp();
-  int b1 = 0, above = 0;
-  if (lane == 0) {
-    int cum = 0;
-    for (int b = 255; b >= 0; --b) {
-      if (cum + (int)hist[b] >= need) { b1 = b; break; }
-      cum += (int)hist[b];
-    }
-    above = cum;
-  }
-  b1 = __shfl_sync(0xffffffffu, b1, 0);
-  above = __shfl_sync(0xffffffffu, above, 0);
+  uint32_t above = 0;
+  const int b1 = warp_find_count(hist, 0u, (uint32_t)need, lane, &above);
   __syncwarp();
   // level 2: low byte among keys with high byte b1
   for (int i = lane; i < 256; i += 32) hist[i] = 0;
@@ -56,20 +87,66 @@ __device__ void select_threshold(const uint16_t* keys, int Kb, int need, uint32_
   for (int j = lane; j < Kb; j += 32)
     if ((keys[j] >> 8) == b1) atomicAdd(&hist[keys[j] & 0xff], 1u);
   __syncwarp();
-  int b2 = 0, above2 = 0;
-  if (lane == 0) {
-    int cum = above;
-    for (int b = 255; b >= 0; --b) {
-      if (cum + (int)hist[b] >= need) { b2 = b; break; }
-      cum += (int)hist[b];
-    }
-    above2 = cum;
-  }
-  b2 = __shfl_sync(0xffffffffu, b2, 0);
-  above2 = __shfl_sync(0xffffffffu, above2, 0);
+  uint32_t above2 = 0;
+  const int b2 = warp_find_count(hist, above, (uint32_t)need, lane, &above2);
   __syncwarp();
   *T_out = (b1 << 8) | b2;
-  *take_eq = need - above2;
+  *take_eq = need - (int)above2;
+}
+
+// Walk the bins from the top while the running mass stays <= thr: returns the
+// first bin where it would exceed thr (-1: none), with the mass and count of the
+// bins above it in *cm, *count (base_* added).
+__device__ __forceinline__ int warp_find_mass(const uint32_t* hist, const unsigned long long* mass,
+                                              unsigned long long base_m, int base_c, uint64_t thr, int lane,
+                                              unsigned long long* cm_out, int* count_out) {
+  const int hi = 255 - 8 * lane;
+  unsigned long long mv[8], mtot = 0;
+  uint32_t hv[8], ctot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    mv[i] = mass[hi - i];
+    hv[i] = hist[hi - i];
+    mtot += mv[i];
+    ctot += hv[i];
+  }
+  unsigned long long mpre = mtot;
+  uint32_t cpre = ctot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const unsigned long long v = __shfl_up_sync(0xffffffffu, mpre, off);
+    const uint32_t c = __shfl_up_sync(0xffffffffu, cpre, off);
+    if (lane >= off) {
+      mpre += v;
+      cpre += c;
+    }
+  }
+  const unsigned over = __ballot_sync(0xffffffffu, base_m + mpre > thr);
+  if (!over) {
+    *cm_out = __shfl_sync(0xffffffffu, base_m + mpre, 31);
+    *count_out = base_c + (int)__shfl_sync(0xffffffffu, cpre, 31);
+    return -1;
+  }
+  const int L = __ffs(over) - 1;
+  unsigned long long cm = base_m + mpre - mtot;
+  int count = base_c + (int)(cpre - ctot);
+  int b = hi - 7;
+  if (lane == L) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (cm + mv[i] <= thr) {
+        cm += mv[i];
+        count += (int)hv[i];
+      } else {
+        b = hi - i;
+        break;
+      }
+    }
+  }
+  b = __shfl_sync(0xffffffffu, b, L);
+  *cm_out = __shfl_sync(0xffffffffu, cm, L);
+  *count_out = __shfl_sync(0xffffffffu, count, L);
+  return b;
 }
 
 // Number of ranks whose cumulative probability (2^-56 fixed point, exact) stays <= thr.
@@ -83,17 +160,9 @@ __device__ int cdf_count(const uint16_t* keys, int Kb, uint64_t thr, uint32_t* h
     atomicAdd(&mass[k >> 8], (unsigned long long)fixed56(bf16_bits_to_f32(k)));
   }
   __syncwarp();
-  int b1 = -1, count = 0;
   unsigned long long cm = 0;
-  if (lane == 0) {
-    for (int b = 255; b >= 0; --b) {
-      if (cm + mass[b] <= thr) { cm += mass[b]; count += (int)hist[b]; }
-      else { b1 = b; break; }
-    }
-  }
-  b1 = __shfl_sync(0xffffffffu, b1, 0);
-  count = __shfl_sync(0xffffffffu, count, 0);
-  cm = __shfl_sync(0xffffffffu, cm, 0);
+  int count = 0;
+  const int b1 = warp_find_mass(hist, mass, 0ull, 0, thr, lane, &cm, &count);
   __syncwarp();
   if (b1 < 0) return Kb;
   for (int i = lane; i < 256; i += 32) { hist[i] = 0; mass[i] = 0ull; }
@@ -106,19 +175,17 @@ __device__ int cdf_count(const uint16_t* keys, int Kb, uint64_t thr, uint32_t* h
     }
   }
   __syncwarp();
-  if (lane == 0) {
-    for (int b = 255; b >= 0; --b) {
-      if (cm + mass[b] <= thr) { cm += mass[b]; count += (int)hist[b]; }
-      else {
-        const uint64_t v = fixed56(bf16_bits_to_f32((uint16_t)((b1 << 8) | b)));
-        const uint64_t extra = (thr - cm) / v;   // v > 0: this bin's mass exceeds thr - cm >= 0
-        count += (int)(extra < hist[b] ? extra : hist[b]);
-        break;
-      }
-    }
+  unsigned long long cm2 = 0;
+  int count2 = 0;
+  const int b = warp_find_mass(hist, mass, cm, count, thr, lane, &cm2, &count2);
+  if (b >= 0) {
+    // the bin where the mass crosses thr: as many of its (equal) keys as still fit
+    const uint64_t v = fixed56(bf16_bits_to_f32((uint16_t)((b1 << 8) | b)));
+    const uint64_t extra = (thr - cm2) / v;   // v > 0: this bin's mass exceeds thr - cm2 >= 0
+    const uint32_t hb = hist[b];
+    count2 += (int)(extra < hb ? extra : hb);
   }
-  count = __shfl_sync(0xffffffffu, count, 0);
-  return count;
+  return count2;
 }
 
 template <int kMaskRows>
