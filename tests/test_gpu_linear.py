@@ -59,6 +59,30 @@ def test_quant_convrot_bit_exact(ops, act, m, k):
     np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), so)
 
 
+def test_quant_act_range_edges_bit_exact(ops):
+    """Input activations at the exponential's range edges: gate values on both sides of
+    the overflow (exp(-g) > FLT_MAX) and underflow bounds, huge, infinite and subnormal
+    values, for the SwiGLU and tanh-GELU quantizers, bit for bit against the oracle."""
+    edges = [-88.0, -88.5, -89.0, -90.0, -100.0, -103.5, -104.0, -119.0, -121.0, -200.0, -3.0e38,
+             88.0, 88.5, 89.0, 103.5, 104.0, 105.0, 120.0, 121.0, 200.0, 3.0e38, float("inf"), float("-inf"),
+             0.0, -0.0, 1e-40, -1e-40, 9.0, 10.0, 11.0, -9.5, -10.5, 0.5, -0.5]
+    k = 256
+    g = torch.Generator().manual_seed(5)
+    rows = []
+    for i in range(0, len(edges), 8):
+        gate = torch.randn(k, generator=g)
+        vals = torch.tensor(edges[i:i + 8])
+        gate[:len(vals)] = vals
+        up = torch.randn(k, generator=g)
+        rows.append(torch.cat([gate, up]))
+    x = torch.stack(rows).to(torch.bfloat16)
+    for act, code, xin in (("swiglu", 2, x), ("gelu_tanh", 1, x[:, :k].contiguous())):
+        q, s = ops.quantize_int8_rowwise_convrot64(xin.cuda(), 256, act)
+        qo, so = O.quant_rowwise_convrot(bits(xin), code)
+        np.testing.assert_array_equal(q.cpu().numpy(), qo, err_msg=act)
+        np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), so, err_msg=act)
+
+
 def test_quant_convrot_strided_rows(ops):
     x = _x(64, 3 * 1024, seed=11)
     xs = x.cuda()[:, 1024:2048]

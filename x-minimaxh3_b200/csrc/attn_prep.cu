@@ -338,16 +338,28 @@ cudaError_t launch_qk_rmsnorm_rope(const QkRopeArgs& a, cudaStream_t s) {
 
 constexpr int kAbsRows = 512;
 
+// Per-column |V| maxima over a band of kAbsRows rows: each thread reads 8
+// consecutive columns (one 16-byte load per row) and keeps 8 running maxima.
 __global__ void __launch_bounds__(256) value_absmax_kernel(const uint16_t* __restrict__ v, int64_t L, int cols,
                                                             int64_t stride, unsigned int* __restrict__ amax_bits) {
-  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  const int c = 8 * (blockIdx.y * blockDim.x + threadIdx.x);
   if (c >= cols) return;
   const int64_t r0 = (int64_t)blockIdx.x * kAbsRows;
   const int64_t r1 = r0 + kAbsRows < L ? r0 + kAbsRows : L;
-  float m = 0.f;
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   const uint16_t* p = v + r0 * stride + c;
-  for (int64_t r = r0; r < r1; ++r, p += stride) m = fmaxf(m, fabsf(bf16_bits_to_f32(*p)));
-  atomicMax(amax_bits + c, __float_as_uint(m));  // non-negative floats order like their bits
+#pragma unroll 4
+  for (int64_t r = r0; r < r1; ++r, p += stride) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m[2 * j] = fmaxf(m[2 * j], fabsf(__uint_as_float(w[j] << 16)));
+      m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(__uint_as_float(w[j] & 0xffff0000u)));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) atomicMax(amax_bits + c + j, __float_as_uint(m[j]));  // non-negative floats order like their bits
 }
 
 // One CTA per (128-token tile, head): read V[128 tokens][128 ch] (bf16) into
@@ -406,7 +418,7 @@ cudaError_t launch_value_fp8(const void* v, int64_t L, int64_t H, int64_t stride
   const int cols = (int)(H * kD);
   cudaError_t e = cudaMemsetAsync(vscale, 0, sizeof(float) * cols, s);
   if (e != cudaSuccess) return e;
-  dim3 g1((unsigned)((L + kAbsRows - 1) / kAbsRows), (cols + 255) / 256);
+  dim3 g1((unsigned)((L + kAbsRows - 1) / kAbsRows), (cols / 8 + 255) / 256);
   value_absmax_kernel<<<g1, 256, 0, s>>>(static_cast<const uint16_t*>(v), L, cols, stride,
                                          static_cast<unsigned int*>(vscale));
   dim3 g2((unsigned)(Lpad / 128), (unsigned)H);

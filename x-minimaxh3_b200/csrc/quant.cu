@@ -31,9 +31,6 @@ __device__ __forceinline__ uint32_t code_byte(float s) {
   const float c = fminf(127.0f, fmaxf(-128.0f, s));
   return __float_as_uint(__fadd_rn(c, 12582912.0f)) & 0xffu;
 }
-__device__ __forceinline__ float swiglu(float gate, float up) {
-  return __fmul_rn(__fdiv_rn(gate, __fadd_rn(1.0f, h3b_expf(-gate))), up);
-}
 
 // Warp shfl_down tree then the same tree over the (zero padded) warp sums:
 // identical to block_tree_sum in the CPU oracle.
@@ -176,6 +173,43 @@ __device__ __forceinline__ float2 gelu_tanh2(float2 v) {
   return mul2(mul2(splat2(0.5f), v), add2(splat2(1.0f), t));
 }
 
+// h3b_expf on both lanes.  For rint(x log2 e) = n in [-125, 127] (|x| below ~86)
+// h3b_expf's two half scalings of p = 2^f (f in [-0.5, 0.5], so p in [0.7, 1.42])
+// are exact and equal one add of n to p's exponent field, which is what this
+// computes (rint by adding 1.5 * 2^23, as rintf; n from the sum's bits).  A lane
+// outside that range, or NaN, takes h3b_expf itself.
+__device__ __forceinline__ float2 h3b_expf_x2(float2 x) {
+  const float kLog2e = 1.44269502162933349609375f;
+  const float kLn2Hi = 0.693145751953125f;
+  const float kLn2Lo = 1.428606765330187045e-06f;
+  const float2 xc = make_float2(fminf(fmaxf(x.x, -120.0f), 100.0f), fminf(fmaxf(x.y, -120.0f), 100.0f));
+  const float2 t = add2(mul2(xc, splat2(kLog2e)), splat2(12582912.0f));
+  const float2 n = sub2(t, splat2(12582912.0f));
+  float2 r = fma2(n, splat2(-kLn2Hi), xc);
+  r = fma2(n, splat2(-kLn2Lo), r);
+  float2 p = splat2(1.0f / 5040.0f);
+  p = fma2(p, r, splat2(1.0f / 720.0f));
+  p = fma2(p, r, splat2(1.0f / 120.0f));
+  p = fma2(p, r, splat2(1.0f / 24.0f));
+  p = fma2(p, r, splat2(1.0f / 6.0f));
+  p = fma2(p, r, splat2(0.5f));
+  p = fma2(p, r, splat2(1.0f));
+  p = fma2(p, r, splat2(1.0f));
+  const int nx = (int)(__float_as_uint(t.x) - 0x4B400000u), ny = (int)(__float_as_uint(t.y) - 0x4B400000u);
+  float2 e;
+  e.x = (nx >= -125 && nx <= 127 && x.x == x.x) ? __uint_as_float(__float_as_uint(p.x) + ((uint32_t)nx << 23))
+                                                 : h3b_expf(x.x);
+  e.y = (ny >= -125 && ny <= 127 && x.y == x.y) ? __uint_as_float(__float_as_uint(p.y) + ((uint32_t)ny << 23))
+                                                 : h3b_expf(x.y);
+  return e;
+}
+// swiglu on both lanes: the scalar swiglu, lane by lane (IEEE quotient per lane)
+__device__ __forceinline__ float2 swiglu2(float2 gate, float2 up) {
+  const float2 e = h3b_expf_x2(make_float2(-gate.x, -gate.y));
+  const float2 den = add2(splat2(1.0f), e);
+  return mul2(make_float2(__fdiv_rn(gate.x, den.x), __fdiv_rn(gate.y, den.y)), up);
+}
+
 __device__ __forceinline__ uint4 ldg4(const uint16_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 // 16 bf16 of chunk-lane x (words wx) and lane y (words wy) -> 16 float2
 __device__ __forceinline__ void unpack16x2(const uint4 (&wx)[2], const uint4 (&wy)[2], float2 (&v)[16]) {
@@ -243,7 +277,7 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t ro
       float2 u[16];
       unpack16x2(cur.u[0], cur.u[1], u);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = make_float2(swiglu(v[j].x, u[j].x), swiglu(v[j].y, u[j].y));
+      for (int j = 0; j < 16; ++j) v[j] = swiglu2(v[j], u[j]);
     } else if (ACT == 1) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = gelu_tanh2(v[j]);
