@@ -146,6 +146,30 @@ def test_gemm_pair_kernel_bit_exact(ops, m, n, k):
     np.testing.assert_array_equal(bits(out), exp)
 
 
+@pytest.mark.parametrize("m,n,ws_kind,with_bias", [(2222, 4104, "channel", True), (4100, 4096, "scalar", False),
+                                                   (3001, 4160, "channel", False)])
+def test_gemm_pair_kernel_gated_residual_bit_exact(ops, m, n, ws_kind, with_bias):
+    """The 2-SM kernel's in-place gated residual (staged 64-column chunks plus the
+    per-row tail chunk when N is not a multiple of 64) against the oracle epilogue
+    on cuBLAS's accumulators; ragged rows, scalar and per-channel weight scales."""
+    k = 1024
+    g = torch.Generator().manual_seed(m + n)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    xs = torch.rand(m, generator=g) * 1e-2 + 1e-4
+    ws = torch.rand(n if ws_kind == "channel" else 1, generator=g) * 1e-3 + 1e-5
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16) if with_bias else None
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    gate = (torch.randn(n, generator=g) * 0.5).to(torch.bfloat16)
+    r = res.cuda()
+    ops.int8_linear_gated_residual_(r, gate.cuda(), a, xs.cuda(), b, ws.cuda(),
+                                    None if bias is None else bias.cuda())
+    acc = torch._int_mm(a, b.t()).cpu().numpy()
+    exp = O.epilogue(acc, xs.numpy(), ws.numpy(), None if bias is None else bias.float().numpy(),
+                     residual=bits(res), gate=bits(gate))
+    np.testing.assert_array_equal(bits(r), exp)
+
+
 @pytest.mark.parametrize("ws_kind", ["channel", "scalar"])
 @pytest.mark.parametrize("with_bias", [True, False])
 def test_linear_epilogue_bit_exact(ops, ws_kind, with_bias):

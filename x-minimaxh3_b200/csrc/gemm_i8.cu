@@ -34,6 +34,8 @@ struct GemmSmem {
   static constexpr int kTotal = kBarOffset + 256 + 1024;  // barriers + alignment slack
 };
 
+// Every loop over the 32 accumulators is fully unrolled (tails guarded per element):
+// a loop bounded by N would index r[] and y[] at run time and put them in local memory.
 __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, int n0, const GemmArgs& a,
                                                 float xs_m, int kind) {
   const int N = a.N;
@@ -44,7 +46,9 @@ __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, 
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
     } else {
-      for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = (int)r[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < N) dst[j] = (int)r[j];
     }
     return;
   }
@@ -59,7 +63,7 @@ __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, 
     y[j] = a.bias ? fmaf(v, w, __ldg(a.bias + nn)) : __fmul_rn(v, w);
   }
   uint16_t* dst = a.out + (int64_t)m * a.out_stride + n0;
-  const bool vec = full && ((a.out_stride & 7) == 0) && ((n0 & 7) == 0);
+  const bool vec = full && ((a.out_stride & 7) == 0) && ((n0 & 7) == 0) && ((uintptr_t)a.out & 15) == 0;
   if (kind == kEpiStore) {
     if (vec) {
 #pragma unroll
@@ -72,7 +76,9 @@ __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, 
         *reinterpret_cast<uint4*>(dst + j) = p;
       }
     } else {
-      for (int j = 0; j < 32 && n0 + j < N; ++j) dst[j] = f32_to_bf16_bits(y[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < N) dst[j] = f32_to_bf16_bits(y[j]);
     }
   } else {  // gated residual, in place
     if (vec) {
@@ -92,7 +98,9 @@ __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, 
         *reinterpret_cast<uint4*>(dst + j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     } else {
-      for (int j = 0; j < 32 && n0 + j < N; ++j) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (n0 + j >= N) continue;
         float rr = bf16_bits_to_f32(dst[j]);
         float g = bf16_bits_to_f32(a.gate[n0 + j]);
         dst[j] = f32_to_bf16_bits(__fadd_rn(rr, __fmul_rn(bf16r(y[j]), g)));
