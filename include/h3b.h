@@ -102,6 +102,24 @@ int h3b_int8_gemm_dequant(const void* A, const void* B, const void* xs, const vo
                           const void* bias, void* D, int64_t M, int64_t N, int64_t K, int64_t out_row_stride,
                           int out_dtype, void* stream);
 
+/* The QKV projection with the q/k head norm and RoPE in its epilogue: D as
+ * h3b_int8_gemm_dequant computes it, and on the Q heads (columns [q_offset,
+ * q_offset + H*128)) and K heads ([k_offset, k_offset + H*128)) of every row the
+ * transform of h3b_qk_rmsnorm_rope applied before the store -- bit-identical to
+ * those two calls in sequence, without the second pass over the rows.
+ * cos_table / sin_table: bf16 [M, rot_dim/2], row m for GEMM row m.
+ * Returns H3B_ERR_UNSUPPORTED with nothing launched unless the shape runs the 2-SM
+ * kernel (ceil(M/256) * ceil(N/256) >= the SM count), rot_dim is 96 or 128, the
+ * offsets are multiples of 128 with both head ranges disjoint and inside N, and D,
+ * the norm weights and the cos/sin tables are 16-byte aligned with
+ * out_row_stride % 8 == 0; the caller then makes the two calls.  Replaces the QKV
+ * projection followed by apply_qknorm_rope (model/layers.py:277-295, 72-149). */
+int h3b_int8_gemm_dequant_qk_rope(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,
+                                  const void* bias, void* D, int64_t M, int64_t N, int64_t K,
+                                  int64_t out_row_stride, int64_t H, int64_t q_offset, int64_t k_offset,
+                                  const void* q_weight, const void* k_weight, const void* cos_table,
+                                  const void* sin_table, int rot_dim, float eps, void* stream);
+
 /* As h3b_int8_gemm_dequant, but the bf16 result y[m,n] is added into a bf16
  * residual stream in place: residual[m,n] = bf16(residual + y * gate[n])
  * (gate: bf16 [N]).  Replaces int8_linear followed by residual.addcmul_

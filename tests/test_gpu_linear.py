@@ -149,9 +149,9 @@ def test_gemm_pair_kernel_bit_exact(ops, m, n, k):
 @pytest.mark.parametrize("m,n,ws_kind,with_bias", [(2222, 4104, "channel", True), (4100, 4096, "scalar", False),
                                                    (3001, 4160, "channel", False)])
 def test_gemm_pair_kernel_gated_residual_bit_exact(ops, m, n, ws_kind, with_bias):
-    """The 2-SM kernel's in-place gated residual (staged 64-column chunks plus the
-    per-row tail chunk when N is not a multiple of 64) against the oracle epilogue
-    on cuBLAS's accumulators; ragged rows, scalar and per-channel weight scales."""
+    """The 2-SM kernel's in-place gated residual (vector 32-column chunks, and the
+    per-element tail when N is not a multiple of 32) against the oracle epilogue on
+    cuBLAS's accumulators; ragged rows, scalar and per-channel weight scales."""
     k = 1024
     g = torch.Generator().manual_seed(m + n)
     a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
@@ -168,6 +168,43 @@ def test_gemm_pair_kernel_gated_residual_bit_exact(ops, m, n, ws_kind, with_bias
     exp = O.epilogue(acc, xs.numpy(), ws.numpy(), None if bias is None else bias.float().numpy(),
                      residual=bits(res), gate=bits(gate))
     np.testing.assert_array_equal(bits(r), exp)
+
+
+@pytest.mark.parametrize("m,heads,rot,ws_kind,with_bias", [
+    (4100, 8, 128, "channel", True),     # 2-SM kernel, ragged last row tile
+    (3100, 8, 96, "scalar", False),      # 2-SM kernel, the real-H3 rotary width
+    (5000, 5, 128, "channel", True),     # 2-SM kernel, a tile holding a Q head and a K head
+    (1000, 8, 128, "channel", True),     # 1-SM shape: the op runs the two kernels instead
+    (3100, 8, 64, "channel", False),     # rotary width the epilogue does not take: two kernels
+])
+def test_qkv_epilogue_qk_rope_bit_exact(ops, m, heads, rot, ws_kind, with_bias):
+    """The QKV GEMM with the q/k RMSNorm + RoPE in its epilogue equals the GEMM
+    followed by the standalone q/k kernel bit for bit, and the oracle on a row sample."""
+    k, W = 1024, heads * 128
+    n = 3 * W
+    g = torch.Generator().manual_seed(m + rot)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int16).to(torch.int8).cuda()
+    xs = (torch.rand(m, generator=g) * 1e-2 + 1e-4).cuda()
+    ws = (torch.rand(n if ws_kind == "channel" else 1, generator=g) * 1e-3 + 1e-5).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda() if with_bias else None
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).cuda()
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).cuda()
+    ang = torch.rand(m, rot // 2, generator=g) * 6
+    ct, st = ang.cos().to(torch.bfloat16).cuda(), ang.sin().to(torch.bfloat16).cuda()
+    ref = ops.int8_linear_prequantized(a, xs, b, ws, bias)
+    ops.qk_rmsnorm_rope_(ref, heads, 0, W, qw, kw, ct, st, 1e-6)
+    got = torch.full((m, n), 7.0, device="cuda", dtype=torch.bfloat16)
+    ops.int8_linear_prequantized_qk_rope(a, xs, b, ws, bias, got, heads, 0, W, qw, kw, ct, st, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    rows = torch.tensor([0, 1, m // 2, m - 2, m - 1])
+    acc = torch._int_mm(a, b.t()).cpu().numpy()[rows.numpy()]
+    y = O.epilogue(acc, xs.cpu().numpy()[rows.numpy()], ws.cpu().numpy(),
+                   None if bias is None else bias.float().cpu().numpy())
+    exp = O.qk_rmsnorm_rope(y, heads, 0, W, bits(qw), bits(kw), bits(ct[rows.cuda()]), bits(st[rows.cuda()]), rot,
+                            1e-6)
+    np.testing.assert_array_equal(bits(got[rows.cuda()]), exp)
 
 
 @pytest.mark.parametrize("ws_kind", ["channel", "scalar"])

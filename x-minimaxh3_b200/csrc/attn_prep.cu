@@ -263,13 +263,6 @@ __device__ __forceinline__ void load4_bf16(const uint16_t* p, bool vec, float (&
   }
 }
 
-// two floats rounded to bf16 (cvt.rn.bf16x2.f32): lo in bits 0..15, hi in 16..31
-__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(QkRopeArgs a) {
   const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;

@@ -114,6 +114,7 @@ static int gemm_common(const void* A, const void* B, int64_t M, int64_t N, int64
   cudaError_t e = cudaSuccess;
   const int r = h3b::launch_gemm(A, B, g, kind, st(stream), &e);
   if (r == 1) return fail(H3B_ERR_CUDA, std::string(what) + ": cuTensorMapEncodeTiled failed");
+  if (r == 4) return fail(H3B_ERR_UNSUPPORTED, std::string(what) + ": the shape does not run the 2-SM kernel");
   return cuda_status(e, what);
 }
 
@@ -132,6 +133,46 @@ int h3b_int8_gemm_dequant(const void* A, const void* B, const void* xs, const vo
   g.out = static_cast<uint16_t*>(D);
   g.out_stride = out_row_stride;
   return gemm_common(A, B, M, N, K, g, 0, stream, "int8_gemm_dequant");
+}
+
+int h3b_int8_gemm_dequant_qk_rope(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,
+                                  const void* bias, void* D, int64_t M, int64_t N, int64_t K,
+                                  int64_t out_row_stride, int64_t H, int64_t q_offset, int64_t k_offset,
+                                  const void* q_weight, const void* k_weight, const void* cos_table,
+                                  const void* sin_table, int rot_dim, float eps, void* stream) {
+  if (!xs || !ws || !D || !q_weight || !k_weight || !cos_table || !sin_table)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ws_numel != 1 && ws_numel != N) return fail(H3B_ERR_INVALID_ARGUMENT, "ws_numel must be 1 or N");
+  if (out_row_stride < N || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "out_row_stride < N or H <= 0");
+  const int64_t W = H * 128;
+  if (rot_dim != 96 && rot_dim != 128)
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_dequant_qk_rope: rot_dim must be 96 or 128");
+  if (q_offset < 0 || k_offset < 0 || q_offset % 128 || k_offset % 128 || q_offset + W > N || k_offset + W > N ||
+      (q_offset < k_offset + W && k_offset < q_offset + W))
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_dequant_qk_rope: head ranges must be disjoint, inside N, at "
+                                     "multiples of 128");
+  if (!aligned16(D) || out_row_stride % 8 || !aligned16(q_weight) || !aligned16(k_weight) ||
+      !aligned16(cos_table) || !aligned16(sin_table))
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_dequant_qk_rope: unaligned operands");
+  if (M > 0 && N > 0 && !h3b::gemm_uses_pair_kernel(M, N))
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_dequant_qk_rope: the shape does not run the 2-SM kernel");
+  h3b::GemmArgs g{};
+  g.xs = static_cast<const float*>(xs);
+  g.ws = static_cast<const float*>(ws);
+  g.ws_scalar = ws_numel == 1;
+  g.bias = static_cast<const float*>(bias);
+  g.out = static_cast<uint16_t*>(D);
+  g.out_stride = out_row_stride;
+  g.q_off = q_offset;
+  g.k_off = k_offset;
+  g.qk_width = W;
+  g.q_norm = static_cast<const uint16_t*>(q_weight);
+  g.k_norm = static_cast<const uint16_t*>(k_weight);
+  g.cos_t = static_cast<const uint16_t*>(cos_table);
+  g.sin_t = static_cast<const uint16_t*>(sin_table);
+  g.qk_eps = eps;
+  return gemm_common(A, B, M, N, K, g, rot_dim == 128 ? h3b::kEpiQkRope64 : h3b::kEpiQkRope48, stream,
+                     "int8_gemm_dequant_qk_rope");
 }
 
 int h3b_int8_gemm_gated_residual(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,

@@ -109,6 +109,89 @@ __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, 
   }
 }
 
+// q/k epilogue of one 128-column head [n_h, n_h + 128) of row m, from its four
+// 32-column accumulator chunks: the bf16 dequantized values (as the store epilogue
+// writes them), then, exactly as qk_rmsnorm_rope_kernel computes them, the head's
+// RMSNorm (sum of squares in the order of that kernel's warp butterfly over 32
+// four-channel groups) and the split-half RoPE of channels [0, 2 * HALF).
+template <int HALF>
+__device__ __forceinline__ void qk_head_finish(uint32_t (&yb)[64], float (&s)[16], int m, int n_h,
+                                               const uint16_t* normw, const GemmArgs& a) {
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) s[i] = __fadd_rn(s[i], s[i + w]);
+  }
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s[0], 0.0078125f), a.qk_eps)));
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(normw + 8 * q));
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t y = yb[4 * q + e];
+      const float v0 = __uint_as_float(y << 16), v1 = __uint_as_float(y & 0xffff0000u);
+      const float w0 = __uint_as_float(ww[e] << 16), w1 = __uint_as_float(ww[e] & 0xffff0000u);
+      yb[4 * q + e] = bf16x2_bits(__fmul_rn(__fmul_rn(v0, inv), w0), __fmul_rn(__fmul_rn(v1, inv), w1));
+    }
+  }
+  const int64_t tok = m < a.M ? m : a.M - 1;  // rows past M (ragged last tile) store nothing
+#pragma unroll
+  for (int q = 0; q < HALF / 8; ++q) {
+    const uint4 cv = __ldg(reinterpret_cast<const uint4*>(a.cos_t + tok * HALF + 8 * q));
+    const uint4 sv = __ldg(reinterpret_cast<const uint4*>(a.sin_t + tok * HALF + 8 * q));
+    const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * q + e, j = i + HALF / 2;  // words of channels (d, d+1) and (d+HALF, d+HALF+1)
+      const float n0 = __uint_as_float(yb[i] << 16), n1 = __uint_as_float(yb[i] & 0xffff0000u);
+      const float p0 = __uint_as_float(yb[j] << 16), p1 = __uint_as_float(yb[j] & 0xffff0000u);
+      const float c0 = __uint_as_float(cw[e] << 16), c1 = __uint_as_float(cw[e] & 0xffff0000u);
+      const float s0 = __uint_as_float(sw[e] << 16), s1 = __uint_as_float(sw[e] & 0xffff0000u);
+      yb[i] = bf16x2_bits(__fsub_rn(__fmul_rn(n0, c0), __fmul_rn(p0, s0)),
+                          __fsub_rn(__fmul_rn(n1, c1), __fmul_rn(p1, s1)));
+      yb[j] = bf16x2_bits(__fadd_rn(__fmul_rn(n0, s0), __fmul_rn(p0, c0)),
+                          __fadd_rn(__fmul_rn(n1, s1), __fmul_rn(p1, c1)));
+    }
+  }
+  if (m < a.M) {
+    uint16_t* dst = a.out + (int64_t)m * a.out_stride + n_h;
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(yb[4 * q], yb[4 * q + 1], yb[4 * q + 2], yb[4 * q + 3]);
+  }
+}
+
+// One 32-column chunk c of a q/k head: bf16 values into yb[16c .. 16c + 15]; the
+// sums of squares g of its eight four-channel groups (groups 8c .. 8c + 7 of 32)
+// go into s: chunks 0, 1 store g, chunks 2, 3 add it (s[i] = g[i] + g[i + 16],
+// the first level of the butterfly tree).
+__device__ __forceinline__ void qk_head_chunk(const uint32_t (&r)[32], int c, int n0, const GemmArgs& a, float xs_m,
+                                              uint32_t (&yb)[64], float (&s)[16]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    float y2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int n = n0 + j + e;
+      const float w = a.ws_scalar ? a.ws[0] : __ldg(a.ws + n);
+      const float v = __fmul_rn((float)(int)r[j + e], xs_m);
+      y2[e] = a.bias ? fmaf(v, w, __ldg(a.bias + n)) : __fmul_rn(v, w);
+    }
+    yb[16 * c + j / 2] = (uint32_t)f32_to_bf16_bits(y2[0]) | ((uint32_t)f32_to_bf16_bits(y2[1]) << 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t lo = yb[16 * c + 2 * i], hi = yb[16 * c + 2 * i + 1];
+    const float v0 = __uint_as_float(lo << 16), v1 = __uint_as_float(lo & 0xffff0000u);
+    const float v2 = __uint_as_float(hi << 16), v3 = __uint_as_float(hi & 0xffff0000u);
+    const float g = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v0, v0), __fmul_rn(v1, v1)), __fmul_rn(v2, v2)),
+                              __fmul_rn(v3, v3));
+    const int gi = (8 * c + i) & 15;
+    s[gi] = c < 2 ? g : __fadd_rn(s[gi], g);
+  }
+}
+
 template <int BN, int KIND>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs a) {
@@ -278,9 +361,28 @@ struct PairSmem {
   static constexpr int kTotal = kBarOffset + 256 + 1024;
 };
 
+// Warp layout of the 2-SM kernel per epilogue kind.  The q/k epilogue does about
+// five times the work per element of the plain store, so it runs 8 epilogue warps
+// (two per TMEM lane quadrant, one 128-column head of the tile each) in warpgroups
+// 1 and 2; warpgroup 0 holds the producer and MMA warps (2 and 3 idle).  Its
+// registers are split with setmaxnreg: warpgroup 0 drops to kQkCtrlRegs, the
+// epilogue warpgroups rise to kQkEpiRegs.  The split must not exceed the launch
+// total; the host checks the compiled register count against kQkLaunchRegs.
+template <int KIND>
+struct PairCfg {
+  static constexpr bool kQk = KIND == kEpiQkRope64 || KIND == kEpiQkRope48;
+  static constexpr int kThreads = kQk ? 384 : kGemmThreads;
+  static constexpr int kEpiWarp0 = kQk ? 4 : 2;
+  static constexpr int kEpiWarps = kQk ? 8 : 4;
+};
+constexpr int kQkLaunchRegs = 168;
+constexpr int kQkCtrlRegs = 72;
+constexpr int kQkEpiRegs = 216;
+static_assert(128 * kQkCtrlRegs + 256 * kQkEpiRegs <= 384 * kQkLaunchRegs, "register split too large");
+
 // The pair tile is 256 x PBN; each CTA's tensor memory holds 2 x PBN columns.
 template <int PBN, int KIND>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThreads, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmArgs a) {
   using S = PairSmem<PBN>;
@@ -311,7 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);
+      mbar_init(&tempty[b], 2 * PairCfg<KIND>::kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -342,6 +444,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const uint32_t full0 = mapa_shared(smem_u32(full), 0);
   const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
 
+  if constexpr (PairCfg<KIND>::kQk) {
+    if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kQkCtrlRegs));
+  }
   if (warp == 0) {
     int stage = 0;
     uint32_t phase = 0;
@@ -399,8 +504,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
-  } else {
-    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4) of this CTA's 128 rows
+  } else if (warp >= PairCfg<KIND>::kEpiWarp0) {
+    if constexpr (PairCfg<KIND>::kQk) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kQkEpiRegs));
+    // epilogue warps -> TMEM lane quadrant (warp % 4) of this CTA's 128 rows
     const int quad = warp & 3;
     const int row_in_tile = (int)rank * 128 + quad * 32 + lane;
     int acc = 0;
@@ -413,19 +519,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int m = mb * 256 + row_in_tile;
       const float xs_m = (KIND != kEpiInt32 && m < a.M) ? __ldg(a.xs + m) : 0.0f;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * PBN);
-#pragma unroll 1
-      for (int c = 0; c < PBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr + (uint32_t)(c * 32), r);
-        tmem_wait_ld();
-        if (c == PBN / 32 - 1) {
-          // this warp is done with the accumulator: release it on the even CTA
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
+      if constexpr (PairCfg<KIND>::kQk) {
+        // this warp's 128-column head of the tile: q/k heads normed and rotated, the rest stored
+        static_assert(PBN == 256, "the q/k epilogue splits a 256-column tile between two warps");
+        const int hh = (warp - PairCfg<KIND>::kEpiWarp0) >> 2;
+        const int n_h = nb * PBN + hh * 128;
+        const bool is_q = n_h >= a.q_off && n_h < a.q_off + a.qk_width;
+        const bool is_k = n_h >= a.k_off && n_h < a.k_off + a.qk_width;
+        uint32_t yb[64];
+        float s[16];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t r[32];
+          tmem_ld32(taddr + (uint32_t)((hh * 4 + c4) * 32), r);
+          tmem_wait_ld();
+          if (c4 == 3) {
+            // this warp is done with the accumulator: release it on the even CTA
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
+          }
+          const int n0 = n_h + c4 * 32;
+          if (is_q || is_k)
+            qk_head_chunk(r, c4, n0, a, xs_m, yb, s);
+          else if (m < a.M && n0 < a.N)
+            epi_store_chunk(r, m, n0, a, xs_m, kEpiStore);
         }
-        const int n0 = nb * PBN + c * 32;
-        if (m < a.M && n0 < a.N) epi_store_chunk(r, m, n0, a, xs_m, KIND);
+        if (is_q || is_k)
+          qk_head_finish<KIND == kEpiQkRope64 ? 64 : 48>(yb, s, m, n_h, is_q ? a.q_norm : a.k_norm, a);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < PBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + (uint32_t)(c * 32), r);
+          tmem_wait_ld();
+          if (c == PBN / 32 - 1) {
+            // this warp is done with the accumulator: release it on the even CTA
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
+          }
+          const int n0 = nb * PBN + c * 32;
+          if (m < a.M && n0 < a.N) epi_store_chunk(r, m, n0, a, xs_m, KIND);
+        }
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
@@ -505,18 +641,30 @@ template <int KIND>
 static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                                     cudaStream_t s) {
   auto k = gemm_i8_pair_kernel<kPairBN, KIND>;
+  if constexpr (PairCfg<KIND>::kQk) {
+    // the register split was planned for kQkLaunchRegs registers per thread at launch
+    cudaFuncAttributes fa;
+    cudaError_t e0 = cudaFuncGetAttributes(&fa, k);
+    if (e0 != cudaSuccess) return e0;
+    if (fa.numRegs != kQkLaunchRegs) return cudaErrorInvalidConfiguration;
+  }
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PairSmem<kPairBN>::kTotal);
   if (e != cudaSuccess) return e;
   const int tiles = ((a.M + 255) / 256) * ((a.N + kPairBN - 1) / kPairBN);
   const int max_pairs = num_sms() / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  k<<<2 * pairs, kGemmThreads, PairSmem<kPairBN>::kTotal, s>>>(ta, tb, a);
+  k<<<2 * pairs, PairCfg<KIND>::kThreads, PairSmem<kPairBN>::kTotal, s>>>(ta, tb, a);
   return cudaGetLastError();
 }
 
-// Returns 0 on success, 1 if a tensor map could not be encoded, else a CUDA error.
+bool gemm_uses_pair_kernel(int64_t M, int64_t N) {
+  return ((M + 255) / 256) * ((N + kPairBN - 1) / kPairBN) >= (int64_t)num_sms();
+}
+
+// Returns 0 on success, 1 if a tensor map could not be encoded, 2 on a CUDA error,
+// 4 if the q/k epilogue was asked for a shape that runs the 1-SM kernel.
 int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t s, cudaError_t* err) {
-  if ((int64_t)((a.M + 255) / 256) * ((a.N + kPairBN - 1) / kPairBN) >= num_sms()) {
+  if (gemm_uses_pair_kernel(a.M, a.N)) {
     // 2-SM kernel: A rows and B rows in boxes of 128 (each CTA's half of a 256 tile)
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K, kBK,
@@ -525,12 +673,15 @@ int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t
     if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, kBK,
                       kPairBN / 2, CU_TENSOR_MAP_SWIZZLE_128B))
       return 1;
-    cudaError_t e = kind == kEpiStore      ? launch_gemm_pair<kEpiStore>(ta, tb, a, s)
-                    : kind == kEpiResidual ? launch_gemm_pair<kEpiResidual>(ta, tb, a, s)
-                                           : launch_gemm_pair<kEpiInt32>(ta, tb, a, s);
+    cudaError_t e = kind == kEpiStore       ? launch_gemm_pair<kEpiStore>(ta, tb, a, s)
+                    : kind == kEpiResidual  ? launch_gemm_pair<kEpiResidual>(ta, tb, a, s)
+                    : kind == kEpiQkRope64  ? launch_gemm_pair<kEpiQkRope64>(ta, tb, a, s)
+                    : kind == kEpiQkRope48  ? launch_gemm_pair<kEpiQkRope48>(ta, tb, a, s)
+                                            : launch_gemm_pair<kEpiInt32>(ta, tb, a, s);
     *err = e;
     return e == cudaSuccess ? 0 : 2;
   }
+  if (kind == kEpiQkRope64 || kind == kEpiQkRope48) return 4;
   const int tiles256 = ((a.M + kBM - 1) / kBM) * ((a.N + 255) / 256);
   const int BN = (tiles256 >= num_sms() || a.N > 128) ? 256 : 128;
   CUtensorMap ta, tb;

@@ -34,6 +34,12 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float bf16r(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+// two floats rounded to bf16 (cvt.rn.bf16x2.f32): lo in bits 0..15, hi in 16..31
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 __device__ __forceinline__ float f16r(float f) { return __half2float(__float2half_rn(f)); }
 
 // Two floats -> two packed e4m3 (satfinite, round to nearest even); lo in bits 0..7.

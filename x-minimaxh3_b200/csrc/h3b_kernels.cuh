@@ -22,7 +22,9 @@ struct QuantArgs {
 cudaError_t launch_quant(const QuantArgs& a, int64_t rows, int mode, bool rms, cudaStream_t s);
 int quant_threads_for(int K);
 
-enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiInt32 = 2 };
+// kEpiQkRope64 / 48: the store epilogue of the QKV projection with the per-head q/k
+// RMSNorm and split-half RoPE (rotary half-width 64 or 48) applied before the store
+enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiInt32 = 2, kEpiQkRope64 = 3, kEpiQkRope48 = 4 };
 struct GemmArgs {
   int M, N, K;
   const float* xs;
@@ -33,8 +35,20 @@ struct GemmArgs {
   int32_t* out_i32;   // raw accumulators
   int64_t out_stride;
   const uint16_t* gate;
+  // q/k norm + RoPE epilogue: q heads at output columns [q_off, q_off + qk_width),
+  // k heads at [k_off, k_off + qk_width), 128 columns each; cos/sin bf16 [rows, half]
+  // for the GEMM's row 0 onwards
+  int64_t q_off, k_off, qk_width;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  const uint16_t* cos_t;
+  const uint16_t* sin_t;
+  float qk_eps;
 };
-// 0 ok, 1 tensor-map encoding failed, 2 CUDA launch error (*err)
+// True when an M x N GEMM runs the 2-SM kernel (the only one with the q/k epilogue).
+bool gemm_uses_pair_kernel(int64_t M, int64_t N);
+// 0 ok, 1 tensor-map encoding failed, 2 CUDA launch error (*err), 4 the q/k epilogue
+// was asked for a shape that does not run the 2-SM kernel
 int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t s, cudaError_t* err);
 bool make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
                   uint64_t rows, uint64_t stride_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw);

@@ -50,6 +50,9 @@ _SIGNATURES = {
                                     c_float, c_int, c_void_p, c_void_p, c_void_p],
     "h3b_int8_gemm_dequant": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                               c_int64, c_int64, c_int, c_void_p],
+    "h3b_int8_gemm_dequant_qk_rope": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+                                      c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_int, c_float, c_void_p],
     "h3b_int8_gemm_gated_residual": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                      c_int64, c_int64, c_int64, c_int64, c_void_p],
     "h3b_int8_gemm_i32": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p],
@@ -73,6 +76,9 @@ _RESTYPES = {"h3b_version": ctypes.c_char_p, "h3b_last_error": ctypes.c_char_p,
              "h3b_key_mean_workspace_bytes": c_int64}
 
 EXPORTED = tuple(_SIGNATURES)
+
+
+H3B_ERR_UNSUPPORTED = -2
 
 
 class H3BError(RuntimeError):

@@ -3,8 +3,9 @@
 Per block (model/layers.py:1074-1298, fused_mlp.py:269-426):
   adaln(t) -> shift/scale/gate x 2           (torch matmul; one GEMV per step)
   xq = rms_adaln + ConvRot + INT8(x)          h3b_rms_adaln_quantize_int8
-  qkv = INT8 GEMM(xq, W_qkv) + bias           h3b_int8_gemm_dequant
-  q, k <- per-head RMSNorm + 3-D RoPE         h3b_qk_rmsnorm_rope
+  qkv = INT8 GEMM(xq, W_qkv) + bias, with    h3b_int8_gemm_dequant_qk_rope (one kernel;
+    q, k <- per-head RMSNorm + 3-D RoPE       h3b_int8_gemm_dequant + h3b_qk_rmsnorm_rope
+    in the epilogue                           for shapes the fused epilogue does not take)
   [Ulysses all-to-all tokens -> heads]        NCCL, only when world > 1
   attention (Sparge-masked quantized)         prep / mask / h3b_attention
   [all-to-all heads -> tokens]
@@ -256,9 +257,8 @@ class DiTBlockB200:
             seg_i = _chunk_segments(segments, r0, r1)
             xq, xs = ops.rms_adaln_quantize_int8(x[r0:r1], self.norm1, scale_a, shift_a, seg_i, cfg.eps,
                                                  self.qkv.convrot_group_size)
-            self.qkv.forward_prequantized(xq, xs, out=qkv[r0:r1])
-            ops.qk_rmsnorm_rope_(qkv[r0:r1], cfg.heads, 0, W, self.q_norm, self.k_norm, rope[0][r0:r1],
-                                 rope[1][r0:r1], cfg.qk_eps)
+            self.qkv.forward_prequantized_qk_rope(xq, xs, qkv[r0:r1], cfg.heads, 0, W, self.q_norm, self.k_norm,
+                                                  rope[0][r0:r1], rope[1][r0:r1], cfg.qk_eps)
         if self.world > 1:
             o = self.attention(P.tokens_to_heads(qkv, cfg.heads, cfg.head_dim, self.group))
             o2 = P.heads_to_tokens(o.view(o.shape[0], -1), Lp, self.group)

@@ -90,11 +90,10 @@ def main() -> None:
     row("rms_adaln + ConvRot INT8 quantizer (K 4096) x2", ms, L * D * 3 + L * 4, "hbm")
     xq, xs = ops.rms_adaln_quantize_int8(x, blk.norm1, sc_a, sh_a, None, cfg.eps, 256)
     qkv = torch.empty(L, 3 * W, device="cuda", dtype=torch.bfloat16)
-    ms = timed(lambda: blk.qkv.forward_prequantized(xq, xs, out=qkv), args.reps)
-    row("QKV INT8 GEMM + dequant (N 12288, K 4096)", ms, 2.0 * L * 3 * W * D, "tensor")
-    ms = timed(lambda: ops.qk_rmsnorm_rope_(qkv, H, 0, W, blk.q_norm, blk.k_norm, rope[0], rope[1], cfg.qk_eps),
-               args.reps)
-    row("q/k RMSNorm + RoPE (in place)", ms, 2 * L * 2 * W * 2, "hbm")
+    ms = timed(lambda: blk.qkv.forward_prequantized_qk_rope(xq, xs, qkv, H, 0, W, blk.q_norm, blk.k_norm, rope[0],
+                                                            rope[1], cfg.qk_eps), args.reps)
+    row("QKV INT8 GEMM + dequant + q/k RMSNorm/RoPE epilogue (N 12288, K 4096)", ms, 2.0 * L * 3 * W * D,
+        "tensor")
     view = qkv.view(L, 3, H, cfg.head_dim)
     q, k, v = view[:, 0], view[:, 1], view[:, 2]
     ms = timed(lambda: A.prepare_values(v), args.reps)

@@ -21,7 +21,7 @@ import ctypes
 
 import torch
 
-from ._lib import check, lib
+from ._lib import H3B_ERR_UNSUPPORTED, check, lib
 
 _ACT_CODES = {None: 0, "none": 0, "gelu_tanh": 1, "swiglu": 2}
 
@@ -216,6 +216,47 @@ def int8_linear_prequantized(xq: torch.Tensor, xs: torch.Tensor, weight: torch.T
     check(lib().h3b_int8_gemm_dequant(_p(xq2), _p(w), _p(xs2), _p(ws), ws.numel(), _p(b), _p(out), M, N, K,
                                       out.stride(0), 2, _stream(xq)), "int8_linear_prequantized")
     return out
+
+
+def int8_linear_prequantized_qk_rope(xq: torch.Tensor, xs: torch.Tensor, weight: torch.Tensor,
+                                     weight_scale: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
+                                     heads: int, q_offset: int, k_offset: int, q_weight: torch.Tensor,
+                                     k_weight: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
+                                     eps: float = 1e-6) -> torch.Tensor:
+    """The QKV projection into `out` with the per-head q/k RMSNorm + split-half RoPE
+    applied in the GEMM epilogue (model/layers.py:277-295 then 72-149).  Bit-identical
+    to int8_linear_prequantized followed by qk_rmsnorm_rope_, which it runs instead
+    when the library reports the shape unsupported by the fused epilogue (GEMMs that
+    take the 1-SM kernel, rotary widths other than 96 and 128)."""
+    _cuda("int8_linear_prequantized_qk_rope", xq, xs, weight, out, q_weight, k_weight, cos_table, sin_table)
+    if weight.dtype != torch.int8 or weight.ndim != 2:
+        raise ValueError("weight must be a rank-two int8 tensor")
+    if out.dtype != torch.bfloat16 or out.ndim != 2 or out.stride(1) != 1:
+        raise ValueError("out must be bfloat16 rows [M, N] with unit column stride")
+    xq2 = xq if xq.is_contiguous() else xq.contiguous()
+    M, K = xq2.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K or tuple(out.shape) != (M, N):
+        raise ValueError(f"shape mismatch: xq {tuple(xq.shape)}, weight {tuple(weight.shape)}, out {tuple(out.shape)}")
+    rot = 2 * cos_table.shape[-1]
+    if cos_table.shape != (M, rot // 2) or sin_table.shape != cos_table.shape:
+        raise ValueError("rotation tables must be [M, rot_dim/2]")
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    ws = _weight_scale(weight_scale, N, xq.device)
+    b = _bias_f32(bias, N, xq.device)
+    xs2 = xs.reshape(-1).to(torch.float32).contiguous()
+    qw = q_weight.to(torch.bfloat16).contiguous()
+    kw = k_weight.to(torch.bfloat16).contiguous()
+    ct = cos_table.to(torch.bfloat16).contiguous()
+    st = sin_table.to(torch.bfloat16).contiguous()
+    status = lib().h3b_int8_gemm_dequant_qk_rope(_p(xq2), _p(w), _p(xs2), _p(ws), ws.numel(), _p(b), _p(out), M, N,
+                                                 K, out.stride(0), heads, q_offset, k_offset, _p(qw), _p(kw), _p(ct),
+                                                 _p(st), rot, float(eps), _stream(xq))
+    if status != H3B_ERR_UNSUPPORTED:
+        check(status, "int8_linear_prequantized_qk_rope")
+        return out
+    int8_linear_prequantized(xq2, xs2, w, ws, b, out=out)
+    return qk_rmsnorm_rope_(out, heads, q_offset, k_offset, qw, kw, ct, st, eps)
 
 
 def _quantize_for_linear(x, convrot, convrot_groupsize, input_act):

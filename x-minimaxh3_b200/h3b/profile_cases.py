@@ -15,6 +15,8 @@ Cases:
     pool_q                     h3b_pool_sim_quant on the queries, L = 65,536, 32 heads, 128-row blocks
     mask                       h3b_block_mask (cdf 0.6 + first column + diagonal), L = 65,536, 32 heads
     qk_rope                    h3b_qk_rmsnorm_rope on QKV rows [65,536, 3 x 4,096], rotary width 128
+    keys                       K mean + pool / similarity / INT8 (prepare_keys), L = 65,536, 32 heads
+    values                     V absmax + FP8 transpose (prepare_values), L = 65,536, 32 heads
 """
 
 from __future__ import annotations
@@ -60,6 +62,9 @@ def _case(name: str, g: torch.Generator):
         sc = (0.1 * torch.randn(4096, device=dev, generator=g)).bfloat16()
         sh = (0.1 * torch.randn(4096, device=dev, generator=g)).bfloat16()
         return lambda: ops.rms_adaln_quantize_int8(x, w, sc, sh, None, 1e-5, 256)
+    if name in ("keys", "values"):
+        x = torch.randn(65536, 32, 128, device=dev, generator=g).bfloat16()
+        return (lambda: A.prepare_keys(x)) if name == "keys" else (lambda: A.prepare_values(x))
     if name in ("pool_q", "mask"):
         L, H = 65536, 32
         q, k = (torch.randn(L, H, 128, device=dev, generator=g).bfloat16() for _ in range(2))

@@ -140,6 +140,19 @@ class _QuantLinear:
         self._correct_(out, xq, xs)
         return out
 
+    def forward_prequantized_qk_rope(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor, heads: int,
+                                     q_offset: int, k_offset: int, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                                     cos_table: torch.Tensor, sin_table: torch.Tensor, eps: float) -> torch.Tensor:
+        """The QKV projection into `out` followed by the per-head q/k RMSNorm + RoPE
+        (model/layers.py:277-295), fused into the GEMM epilogue when this layer has no
+        post-GEMM correction; the same values either way."""
+        if getattr(self, "correction", None) is None:
+            w8, ws = self.int8_weight()
+            return ops.int8_linear_prequantized_qk_rope(xq, xs, w8, ws, self.bias, out, heads, q_offset, k_offset,
+                                                        q_weight, k_weight, cos_table, sin_table, eps)
+        self.forward_prequantized(xq, xs, out=out)
+        return ops.qk_rmsnorm_rope_(out, heads, q_offset, k_offset, q_weight, k_weight, cos_table, sin_table, eps)
+
     def gated_residual_(self, residual: torch.Tensor, gate: torch.Tensor, xq: torch.Tensor,
                         xs: torch.Tensor) -> torch.Tensor:
         """residual += bf16(layer(x)) * gate with one bf16 rounding (model/layers.py:944-960)."""
