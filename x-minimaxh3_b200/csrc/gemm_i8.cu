@@ -349,8 +349,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //               CTA's full barrier (count 2 + bytes)
 //   warp 1      pair TMEM allocation in both CTAs; MMA issuer in the even CTA,
 //               whose commits arrive on both CTAs' barriers (empty, tfull)
-//   warps 2..5  epilogue in both CTAs; each warp releases the accumulator on the
-//               even CTA's tempty barrier (count 8: 4 warps x 2 CTAs)
+//   epilogue    in both CTAs (warps 4..11, two per TMEM lane quadrant, for the
+//               bf16 kinds; warps 2..5 for the int32 kind, see PairCfg); each
+//               warp releases the accumulator on the even CTA's tempty barrier
+//               (count: epilogue warps x 2 CTAs)
 template <int PBN>
 struct PairSmem {
   static constexpr int kStages = PBN == 256 ? 6 : 8;
@@ -361,19 +363,23 @@ struct PairSmem {
   static constexpr int kTotal = kBarOffset + 256 + 1024;
 };
 
-// Warp layout of the 2-SM kernel per epilogue kind.  The q/k epilogue does about
-// five times the work per element of the plain store, so it runs 8 epilogue warps
-// (two per TMEM lane quadrant, one 128-column head of the tile each) in warpgroups
-// 1 and 2; warpgroup 0 holds the producer and MMA warps (2 and 3 idle).  Its
-// registers are split with setmaxnreg: warpgroup 0 drops to kQkCtrlRegs, the
-// epilogue warpgroups rise to kQkEpiRegs.  The split must not exceed the launch
-// total; the host checks the compiled register count against kQkLaunchRegs.
+// Warp layout of the 2-SM kernel per epilogue kind.  The bf16 epilogues (store,
+// gated residual, q/k norm + RoPE) run 8 epilogue warps, two per TMEM lane
+// quadrant, each taking one 128-column half of the tile, in warpgroups 1 and 2;
+// warpgroup 0 holds the producer and MMA warps (2 and 3 idle).  With one warp per
+// quadrant the epilogue is latency-bound and, at K = 4096, slower than the MMAs of
+// the next tile.  Registers are split with setmaxnreg: warpgroup 0 drops to
+// kQkCtrlRegs, the epilogue warpgroups rise to kQkEpiRegs.  The split must not
+// exceed the launch total; the host checks the compiled register count against
+// kQkLaunchRegs.  The int32 verification kind keeps 192 threads, one epilogue warp
+// per quadrant.
 template <int KIND>
 struct PairCfg {
   static constexpr bool kQk = KIND == kEpiQkRope64 || KIND == kEpiQkRope48;
-  static constexpr int kThreads = kQk ? 384 : kGemmThreads;
-  static constexpr int kEpiWarp0 = kQk ? 4 : 2;
-  static constexpr int kEpiWarps = kQk ? 8 : 4;
+  static constexpr bool kWide = kQk || KIND == kEpiResidual || KIND == kEpiStore;
+  static constexpr int kThreads = kWide ? 384 : kGemmThreads;
+  static constexpr int kEpiWarp0 = kWide ? 4 : 2;
+  static constexpr int kEpiWarps = kWide ? 8 : 4;
 };
 constexpr int kQkLaunchRegs = 168;
 constexpr int kQkCtrlRegs = 72;
@@ -444,7 +450,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThre
   const uint32_t full0 = mapa_shared(smem_u32(full), 0);
   const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
 
-  if constexpr (PairCfg<KIND>::kQk) {
+  if constexpr (PairCfg<KIND>::kWide) {
     if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kQkCtrlRegs));
   }
   if (warp == 0) {
@@ -505,7 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThre
       }
     }
   } else if (warp >= PairCfg<KIND>::kEpiWarp0) {
-    if constexpr (PairCfg<KIND>::kQk) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kQkEpiRegs));
+    if constexpr (PairCfg<KIND>::kWide) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kQkEpiRegs));
     // epilogue warps -> TMEM lane quadrant (warp % 4) of this CTA's 128 rows
     const int quad = warp & 3;
     const int row_in_tile = (int)rank * 128 + quad * 32 + lane;
@@ -547,6 +553,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThre
         }
         if (is_q || is_k)
           qk_head_finish<KIND == kEpiQkRope64 ? 64 : 48>(yb, s, m, n_h, is_q ? a.q_norm : a.k_norm, a);
+      } else if constexpr (PairCfg<KIND>::kWide) {
+        // this warp's 128-column half of the tile
+        const int hh = (warp - PairCfg<KIND>::kEpiWarp0) >> 2;
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const int c = hh * 4 + c4;
+          uint32_t r[32];
+          tmem_ld32(taddr + (uint32_t)(c * 32), r);
+          tmem_wait_ld();
+          if (c4 == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
+          }
+          const int n0 = nb * PBN + c * 32;
+          if (m < a.M && n0 < a.N) epi_store_chunk(r, m, n0, a, xs_m, KIND);
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < PBN / 32; ++c) {
@@ -641,7 +664,7 @@ template <int KIND>
 static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                                     cudaStream_t s) {
   auto k = gemm_i8_pair_kernel<kPairBN, KIND>;
-  if constexpr (PairCfg<KIND>::kQk) {
+  if constexpr (PairCfg<KIND>::kWide) {
     // the register split was planned for kQkLaunchRegs registers per thread at launch
     cudaFuncAttributes fa;
     cudaError_t e0 = cudaFuncGetAttributes(&fa, k);
