@@ -69,6 +69,35 @@ __device__ __forceinline__ int warp_find_count(const uint32_t* hist, uint32_t ba
   return b;
 }
 
+// First-level count + mass histogram update for one warp step (one key per lane;
+// lanes past the end pass valid = false).  The probabilities of a row mostly share
+// a few high bytes, so per-key 64-bit atomics would collide 32 ways.  Instead each
+// distinct bin of the step is added once: the lowest pending lane's bin, its lanes
+// by ballot, the count by popc and the lanes' fixed-point masses (each < 2^57) as
+// three exact 24 / 24 / 9-bit warp sums.  Integer sums, so the totals equal the
+// per-key atomics' in any order.  (The count-only histogram of select_threshold
+// keeps per-key 32-bit atomics: measured faster there.)
+template <bool MASS>
+__device__ __forceinline__ void hist_add_by_bin(uint32_t* hist, unsigned long long* mass, int bin, bool valid,
+                                                uint64_t m, int lane) {
+  uint32_t pending = __ballot_sync(0xffffffffu, valid);
+  while (pending) {
+    const int leader = __ffs(pending) - 1;
+    const int lb = __shfl_sync(0xffffffffu, bin, leader);
+    const bool mine = valid && bin == lb;
+    const uint32_t peers = __ballot_sync(0xffffffffu, mine);
+    if constexpr (MASS) {
+      const uint32_t lo = __reduce_add_sync(0xffffffffu, mine ? (uint32_t)(m & 0xffffffu) : 0u);
+      const uint32_t mid = __reduce_add_sync(0xffffffffu, mine ? (uint32_t)((m >> 24) & 0xffffffu) : 0u);
+      const uint32_t hi = __reduce_add_sync(0xffffffffu, mine ? (uint32_t)(m >> 48) : 0u);
+      if (lane == leader)
+        atomicAdd(&mass[lb], (unsigned long long)lo + ((unsigned long long)mid << 24) + ((unsigned long long)hi << 48));
+    }
+    if (lane == leader) atomicAdd(&hist[lb], (uint32_t)__popc(peers));
+    pending &= ~peers;
+  }
+}
+
 // Threshold key T and how many of the keys equal to T to keep, so that exactly
 // `need` keys are kept (keys > T all kept).  hist: per-warp shared counters.
 __device__ void select_threshold(const uint16_t* keys, int Kb, int need, uint32_t* hist, int lane, int* T_out,
@@ -154,10 +183,11 @@ __device__ int cdf_count(const uint16_t* keys, int Kb, uint64_t thr, uint32_t* h
                          int lane) {
   for (int i = lane; i < 256; i += 32) { hist[i] = 0; mass[i] = 0ull; }
   __syncwarp();
-  for (int j = lane; j < Kb; j += 32) {
-    const uint16_t k = keys[j];
-    atomicAdd(&hist[k >> 8], 1u);
-    atomicAdd(&mass[k >> 8], (unsigned long long)fixed56(bf16_bits_to_f32(k)));
+  for (int j0 = 0; j0 < Kb; j0 += 32) {
+    const int j = j0 + lane;
+    const bool valid = j < Kb;
+    const uint16_t k = valid ? keys[j] : (uint16_t)0;
+    hist_add_by_bin<true>(hist, mass, k >> 8, valid, valid ? fixed56(bf16_bits_to_f32(k)) : 0ull, lane);
   }
   __syncwarp();
   unsigned long long cm = 0;
