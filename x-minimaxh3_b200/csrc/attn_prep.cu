@@ -134,8 +134,14 @@ __device__ __forceinline__ void load4_row(const PoolArgs& a, int64_t row, int h,
 }
 
 // One CTA of four warps per (block, head); lane l owns channels 4l..4l+3 and
-// warp w walks rows w, w+4, ... of the block.
+// warp w walks rows w, w+4, ... of the block.  With a mean (keys), the first pass
+// keeps each row's mean-subtracted bf16 values in shared memory (blk x 256 bytes,
+// dynamic) and the quantizing pass reads them back from there (the same thread
+// wrote them) instead of reloading and recomputing them.  Without one (queries,
+// 128-row blocks) the quantizing pass reloads: the 32 KB a CTA would need costs
+// more occupancy than the reload.
 __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
+  extern __shared__ uint2 rows_s[];  // [blk][32]: lane l's four bf16 of each row
   __shared__ float pp_s[4][kD], sp_s[4][kD];
   __shared__ float amax_s[4];
   __shared__ float scale_s;
@@ -159,6 +165,9 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
   for (int r = warp; r < valid; r += 4) {
     float v[4];
     load4_row(a, r0 + r, h, lane, mean4, v);
+    if (a.mean)
+      rows_s[r * 32 + lane] = make_uint2((__float_as_uint(v[0]) >> 16) | (__float_as_uint(v[1]) & 0xffff0000u),
+                                       (__float_as_uint(v[2]) >> 16) | (__float_as_uint(v[3]) & 0xffff0000u));
     float sq = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])), __fmul_rn(v[2], v[2])),
                          __fmul_rn(v[3], v[3]));
     const float norm = __fsqrt_rn(warp_butterfly_sum(sq));
@@ -219,7 +228,15 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
     uint32_t word = 0;
     if (r < valid) {
       float v[4];
-      load4_row(a, r0 + r, h, lane, mean4, v);
+      if (a.mean) {
+        const uint2 raw = rows_s[r * 32 + lane];
+        v[0] = __uint_as_float(raw.x << 16);
+        v[1] = __uint_as_float(raw.x & 0xffff0000u);
+        v[2] = __uint_as_float(raw.y << 16);
+        v[3] = __uint_as_float(raw.y & 0xffff0000u);
+      } else {
+        load4_row(a, r0 + r, h, lane, mean4, v);
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float t = div_rn_by(v[i], sc, rsc);
@@ -237,7 +254,7 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
 cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s) {
   const int nb = (int)((a.L + a.blk - 1) / a.blk);
   dim3 grid(nb, a.H);
-  pool_sim_quant_kernel<<<grid, 128, 0, s>>>(a);
+  pool_sim_quant_kernel<<<grid, 128, a.mean ? (size_t)a.blk * 32 * sizeof(uint2) : 0, s>>>(a);
   return cudaGetLastError();
 }
 
