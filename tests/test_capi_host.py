@@ -56,6 +56,30 @@ def test_unsupported_shapes_are_rejected():
                                0.1, dummy, 128, None) == -2
 
 
+def test_qkv_qk_rope_entry_rejects_what_it_does_not_take():
+    """The fused QKV + q/k norm/RoPE entry answers 'unsupported' (-2) for the cases its
+    caller must route to the two-call path, and 'invalid' (-1) for bad arguments, all
+    before any CUDA call."""
+    d, odd = ctypes.c_void_p(16), ctypes.c_void_p(18)
+
+    def call(D=d, ws_numel=1, M=4096, N=3072, stride=3072, H=8, q_off=0, k_off=1024, rot=128, qw=d):
+        return lib().h3b_int8_gemm_dequant_qk_rope(d, d, d, d, ws_numel, None, D, M, N, 256, stride, H, q_off,
+                                                   k_off, qw, d, d, d, rot, 1e-6, None)
+
+    assert call(rot=64) == -2                      # rotary width without a fused epilogue
+    assert call(k_off=512) == -2                   # Q and K head ranges overlap
+    assert call(k_off=2560) == -2                  # K heads run past N
+    assert call(q_off=64) == -2                    # head not at a 128-column boundary
+    assert call(D=odd) == -2                       # unaligned output rows
+    assert call(stride=3076) == -2                 # row stride not a multiple of 8
+    assert call(ws_numel=7) == -1
+    assert call(qw=None) == -1
+    assert call(H=0) == -1
+    assert b"H <= 0" in lib().h3b_last_error()
+    assert call(rot=64) == -2
+    assert b"rot_dim" in lib().h3b_last_error()
+
+
 def test_empty_inputs_are_no_ops():
     assert lib().h3b_quantize_int8_rowwise(None, 0, 256, 256, None, None, None) == 0
     assert lib().h3b_int8_gemm_dequant(None, None, ctypes.c_void_p(16), ctypes.c_void_p(16), 1, None,
