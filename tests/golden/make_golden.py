@@ -22,6 +22,9 @@ reference function that produced it:
                       torch_sdpa attention; model/assembly.py:259-333, layers.py:996-1298) over
                       the synthetic checkpoint of tests/golden/h3_checkpoint.py, plus each
                       layer's output on a seeded input and the layer class / spec chosen
+  qk_rope.npz         apply_qknorm_rope on CPU bf16 tensors with the engine's packed split-half
+                      rotation table (model/layers.py:60-118: rope_rotation_table, F.rms_norm,
+                      rotate_table), rotary widths 128 and 96
   mask_topk.npz       SplitModalityProtectedSpargeAttentionBackend.long_sequence_video_queries
                       (model/kernels.py:3668-3997) with the two absent Sparge helpers replaced
                       by recorders (fill: set the first `count` sorted indices; LUT: capture
@@ -197,6 +200,29 @@ def gen_sparge():
          qb=qb[0].numpy(), sbs=sbs[0].numpy())
 
 
+def gen_qk_rope():
+    from h3serve.native_engine.model.layers import apply_qknorm_rope, rope_rotation_table
+
+    g = torch.Generator().manual_seed(72)
+    L, H = 67, 3
+    arrays = {}
+    for rot in (128, 96):
+        q = (torch.randn(L, H, 128, generator=g) * 2).to(torch.bfloat16)
+        k = (torch.randn(L, H, 128, generator=g) * 2 + 0.5).to(torch.bfloat16)
+        qw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+        kw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+        angles = torch.rand(L, rot, generator=g) * 6        # split-half: the first rot/2 are used
+        table = rope_rotation_table(angles, torch.bfloat16)
+        qo, ko = apply_qknorm_rope(q, k, q_weight=qw, k_weight=kw, frequencies=table, eps=1e-6)
+        half = rot // 2
+        arrays.update({f"r{rot}_q": bits(q), f"r{rot}_k": bits(k), f"r{rot}_qw": bits(qw), f"r{rot}_kw": bits(kw),
+                       f"r{rot}_cos": bits(table[0, :, 0, :, 0, 0].contiguous()),
+                       f"r{rot}_sin": bits(table[0, :, 0, :, 1, 0].contiguous()),
+                       f"r{rot}_qo": bits(qo), f"r{rot}_ko": bits(ko)})
+        assert table.shape[3] == half
+    save("qk_rope.npz", **arrays)
+
+
 def gen_lut():
     from h3serve.native_engine.model.sparse_lut import _parallel_lut_kernels
 
@@ -342,6 +368,7 @@ def gen_block_ckpt():
 if __name__ == "__main__":
     torch.manual_seed(0)
     only = sys.argv[2:]
-    for fn in (gen_quant, gen_convrot, gen_act, gen_w4, gen_linear, gen_sparge, gen_lut, gen_mask, gen_block_ckpt):
+    for fn in (gen_quant, gen_convrot, gen_act, gen_w4, gen_linear, gen_sparge, gen_lut, gen_mask, gen_block_ckpt,
+               gen_qk_rope):
         if not only or fn.__name__ in only:
             fn()

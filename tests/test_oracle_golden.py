@@ -187,3 +187,35 @@ def test_fixed_topk_mask_matches_reference_selector():
             bm = O.block_mask(pq, sq, pk, sk, mode=0, budget=topk / 100.0, protected_kb=(prot + 63) // 64)
             got = O.bitmap_to_bool(bm, Kb)
             np.testing.assert_array_equal(got, z[f"topk{topk}_prot{prot}"], err_msg=f"topk{topk} prot{prot}")
+
+
+@pytest.mark.parametrize("rot", [128, 96])
+def test_qk_rmsnorm_rope_vs_reference_cpu_path(rot):
+    """apply_qknorm_rope on CPU bf16 tensors with the engine's packed rotation table
+    (model/layers.py:60-118).  The per-head RMSNorm agrees bit for bit (the channels past
+    the rotary width).  The rotated channels differ by rounding only: the reference's CPU
+    path rounds each product to bf16 before the bf16 sum, while the oracle (like the
+    reference's fused CUDA kernel, rms_rope.cu) keeps fp32 until one final rounding.  So
+    each rotated output stays within 2^-6 of |n_d| |cos| + |n_e| |sin|, the magnitudes of
+    its two products (measured at most 2^-7)."""
+    z = load("qk_rope.npz")
+    q, k = z[f"r{rot}_q"], z[f"r{rot}_k"]
+    L, H, D = q.shape
+    half = rot // 2
+    qkv = np.zeros((L, 3 * H * D), np.uint16)
+    qkv[:, :H * D] = q.reshape(L, -1)
+    qkv[:, H * D:2 * H * D] = k.reshape(L, -1)
+    out = O.qk_rmsnorm_rope(qkv, H, 0, H * D, z[f"r{rot}_qw"], z[f"r{rot}_kw"], z[f"r{rot}_cos"],
+                            z[f"r{rot}_sin"], rot, 1e-6)
+    c = bf(z[f"r{rot}_cos"])[:, None, :].astype(np.float64)
+    s = bf(z[f"r{rot}_sin"])[:, None, :].astype(np.float64)
+    for x, w, cols, ref in ((q, z[f"r{rot}_qw"], slice(0, H * D), z[f"r{rot}_qo"]),
+                            (k, z[f"r{rot}_kw"], slice(H * D, 2 * H * D), z[f"r{rot}_ko"])):
+        got = out[:, cols].reshape(L, H, D)
+        np.testing.assert_array_equal(got[..., rot:], ref[..., rot:])
+        xf = bf(x).astype(np.float64)
+        n = xf / np.sqrt((xf ** 2).mean(-1, keepdims=True) + 1e-6) * bf(w)
+        first, second = n[..., :half], n[..., half:rot]
+        scale = np.concatenate((np.abs(first * c) + np.abs(second * s), np.abs(first * s) + np.abs(second * c)), -1)
+        err = np.abs(bf(got[..., :rot]).astype(np.float64) - bf(ref[..., :rot]))
+        assert (err <= 2.0 ** -6 * scale).all(), float((err / scale).max())
