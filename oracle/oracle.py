@@ -107,6 +107,20 @@ def fht256(v: np.ndarray) -> np.ndarray:
     return out.reshape(np.shape(v))
 
 
+def rms_adaln_rows(x_bf16, w_bf16, scale_tab_bf16, shift_tab_bf16, seg_row=None, eps=1e-5):
+    """The modulated rows the fused quantizer rotates and quantizes (bf16 values as float32)."""
+    x = _c(x_bf16, np.uint16)
+    M, K = x.shape
+    w = _c(w_bf16, np.uint16)
+    sc = _c(np.atleast_2d(scale_tab_bf16), np.uint16)
+    sh = _c(np.atleast_2d(shift_tab_bf16), np.uint16)
+    out = np.empty((M, K), np.float32)
+    for m in range(M):
+        r = 0 if seg_row is None else int(seg_row[m])
+        lib().h3bo_rms_adaln_row(_p(x[m]), I64(K), _p(w), _p(sc[r]), _p(sh[r]), ctypes.c_float(eps), _p(out[m]))
+    return out
+
+
 def rms_adaln_quant(x_bf16, w_bf16, scale_tab_bf16, shift_tab_bf16, seg_row=None, eps=1e-5,
                     convrot=True):
     x = _c(x_bf16, np.uint16)

@@ -22,6 +22,9 @@ reference function that produced it:
                       torch_sdpa attention; model/assembly.py:259-333, layers.py:996-1298) over
                       the synthetic checkpoint of tests/golden/h3_checkpoint.py, plus each
                       layer's output on a seeded input and the layer class / spec chosen
+  rms_adaln.npz       RMSNorm module (F.rms_norm) + kernels.rms_adaln's eager segmented
+                      modulation on CPU bf16 rows (model/layers.py:33-49, kernels.py:7594-7642),
+                      hidden 5376 and 4096, three modulation segments
   qk_rope.npz         apply_qknorm_rope on CPU bf16 tensors with the engine's packed split-half
                       rotation table (model/layers.py:60-118: rope_rotation_table, F.rms_norm,
                       rotate_table), rotary widths 128 and 96
@@ -200,6 +203,30 @@ def gen_sparge():
          qb=qb[0].numpy(), sbs=sbs[0].numpy())
 
 
+def gen_rms_adaln():
+    from h3serve.native_engine.model.kernels import rms_adaln
+    from h3serve.native_engine.model.layers import RMSNorm
+
+    g = torch.Generator().manual_seed(94)
+    arrays = {}
+    for K in (5376, 4096):
+        rows = 16
+        x = (torch.randn(rows, K, generator=g) * 2).to(torch.bfloat16)
+        x[5] *= 40.0                                            # a row far from unit scale
+        norm = RMSNorm(K, eps=1e-5, dtype=torch.bfloat16)
+        with torch.no_grad():
+            norm.weight.copy_((1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16))
+        scale = (0.2 * torch.randn(3, K, generator=g)).to(torch.bfloat16)
+        shift = (0.2 * torch.randn(3, K, generator=g)).to(torch.bfloat16)
+        segments = ((0, 4, 2), (4, 9, 0), (9, rows, 1))
+        with torch.no_grad():
+            out = rms_adaln(x.clone(), norm, shift, scale, segments)
+        arrays.update({f"k{K}_x": bits(x), f"k{K}_w": bits(norm.weight.detach()), f"k{K}_scale": bits(scale),
+                       f"k{K}_shift": bits(shift), f"k{K}_segments": np.array(segments, np.int64),
+                       f"k{K}_out": bits(out)})
+    save("rms_adaln.npz", **arrays)
+
+
 def gen_qk_rope():
     from h3serve.native_engine.model.layers import apply_qknorm_rope, rope_rotation_table
 
@@ -369,6 +396,6 @@ if __name__ == "__main__":
     torch.manual_seed(0)
     only = sys.argv[2:]
     for fn in (gen_quant, gen_convrot, gen_act, gen_w4, gen_linear, gen_sparge, gen_lut, gen_mask, gen_block_ckpt,
-               gen_qk_rope):
+               gen_qk_rope, gen_rms_adaln):
         if not only or fn.__name__ in only:
             fn()

@@ -219,3 +219,27 @@ def test_qk_rmsnorm_rope_vs_reference_cpu_path(rot):
         scale = np.concatenate((np.abs(first * c) + np.abs(second * s), np.abs(first * s) + np.abs(second * c)), -1)
         err = np.abs(bf(got[..., :rot]).astype(np.float64) - bf(ref[..., :rot]))
         assert (err <= 2.0 ** -6 * scale).all(), float((err / scale).max())
+
+
+@pytest.mark.parametrize("K", [4096, 5376])
+def test_rms_adaln_rows_vs_reference_eager(K):
+    """RMSNorm module (F.rms_norm) + kernels.rms_adaln's eager segmented modulation on CPU
+    bf16 rows, three segments (model/layers.py:33-49, kernels.py:7594-7642): the modulated
+    rows the fused quantizer rotates, bit-exact on this fixture, and the fused oracle
+    quantizer's codes and scales equal its ConvRot quantizer applied to the reference's rows.
+    The fp32 sum of squares depends on the summation order (torch's reduction against the
+    kernel's fixed tree): on other rows 1 / rms can move by an ulp and leave a value up to
+    2 bf16 steps apart (a 48-row sample at K = 5376 showed 5 such values of 258,048)."""
+    z = load("rms_adaln.npz")
+    x = z[f"k{K}_x"]
+    seg_row = np.zeros(x.shape[0], np.int32)
+    for start, stop, r in z[f"k{K}_segments"]:
+        seg_row[start:stop] = r
+    rows = O.rms_adaln_rows(x, z[f"k{K}_w"], z[f"k{K}_scale"], z[f"k{K}_shift"], seg_row, 1e-5)
+    assert not (rows.view(np.uint32) & 0xFFFF).any(), "modulated rows must be bf16 values"
+    ref = z[f"k{K}_out"]
+    np.testing.assert_array_equal((rows.view(np.uint32) >> 16).astype(np.uint16), ref)
+    q1, s1 = O.rms_adaln_quant(x, z[f"k{K}_w"], z[f"k{K}_scale"], z[f"k{K}_shift"], seg_row, 1e-5, True)
+    q2, s2 = O.quant_rowwise_convrot(ref, 0)
+    np.testing.assert_array_equal(q1, q2)
+    np.testing.assert_array_equal(s1, s2)
