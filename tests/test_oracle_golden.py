@@ -243,3 +243,37 @@ def test_rms_adaln_rows_vs_reference_eager(K):
     q2, s2 = O.quant_rowwise_convrot(ref, 0)
     np.testing.assert_array_equal(q1, q2)
     np.testing.assert_array_equal(s1, s2)
+
+
+def test_value_fp8_vs_reference_formula_in_torch():
+    """V -> FP8 (model/compact_fp8.py:253-300 host part, 13-97 kernel math): per (head,
+    channel) absmax by aminmax, scaled = float(v) * (2.25 / absmax) in fp32, then E4M3 with
+    round-to-nearest (the kernel's cvt.rn.satfinite; |scaled| <= 2.25, so torch's
+    float8_e4m3fn cast rounds identically), scale = absmax / 2.25.  The factor is the IEEE
+    quotient, as everywhere in this build (torch's scalar `2.25 / t` multiplies by a rounded
+    reciprocal and the reference's Triton `/` is not correctly rounded either; either can
+    move a near-tie to the neighbouring code).  The oracle's bytes, transposed to
+    [H, 128, Lpad] without the sm89 16-row permutation, equal torch's.  An all-zero channel
+    gets zeros and scale 0 (the reference would divide by zero)."""
+    import torch
+
+    g = torch.Generator().manual_seed(31)
+    L, H = 300, 3
+    v = (torch.randn(L, H, 128, generator=g) * torch.rand(1, H, 128, generator=g) * 4).to(torch.bfloat16)
+    v[:, 1, 7] = 0                                          # an all-zero channel
+    vt, vs = O.value_fp8(v.contiguous().view(torch.int16).numpy().view(np.uint16))
+    hnd = v.permute(1, 0, 2).float()                        # [H, L, 128]
+    mn, mx = torch.aminmax(hnd, dim=1)
+    absmax = torch.maximum(mn.abs(), mx.abs())
+    factor = torch.full_like(absmax, 2.25) / absmax        # IEEE quotient (tensor / tensor)
+    scaled = hnd * factor[:, None, :]
+    ref = scaled.to(torch.float8_e4m3fn).view(torch.uint8).permute(0, 2, 1).numpy()   # [H, 128, L]
+    live = absmax.numpy() > 0
+    for h in range(H):
+        for d in range(128):
+            if live[h, d]:
+                np.testing.assert_array_equal(vt[h, d, :L], ref[h, d])
+            else:
+                assert not vt[h, d].any() and vs[h, d] == 0
+    np.testing.assert_array_equal(vs[live], (absmax / 2.25).numpy()[live])
+    assert not vt[:, :, L:].any()
