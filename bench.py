@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--impl", choices=("h3b", "reference"), default="h3b")
     ap.add_argument("--tokens", type=int, default=0, help="override L (must divide by the GPU count)")
     ap.add_argument("--grid", type=str, default="", help="latent video grid T,H,W (default 31,45,80 = 720p/5 s; "
-                    "91,68,120 = 1080p/15 s, BASELINE config 5); L is its product unless --tokens is given")
+                    "91,68,120 = 1080p/15 s); L is its product unless --tokens is given")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()

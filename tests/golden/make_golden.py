@@ -153,7 +153,7 @@ def gen_linear():
     out_eager_rot = int8_linear(x, wq, ws, bias, torch.bfloat16, convrot=True, convrot_groupsize=256)
     mod = ConvRotInt8Linear(wq, ws, bias, spec=ComfyQuantSpec("int8_tensorwise", True, 256))
     out_module_rot = mod(x)
-    # W4A8: symmetric int4 groups of 128 (BASELINE), s_rel = group/channel scale in fp32
+    # W4A8: symmetric int4 groups of 128 (the benchmark format), s_rel = group/channel scale in fp32
     G = 128
     wg = (torch.randn(N, K, generator=g) * 0.02).view(N, K // G, G)
     gscale = wg.abs().amax(-1) / 7.0

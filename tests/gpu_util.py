@@ -26,7 +26,8 @@ def cosine(a, b) -> float:
 
 
 def outlier_activations(g, m, k, frac=0.01, mult=20.0):
-    """BASELINE config-1 activations: N(0,1) with 1% of channels scaled by 20."""
+    """Activations with outlier channels, as the INT8 GEMM benchmark uses: N(0,1) with 1% of
+    channels scaled by 20."""
     x = torch.randn(m, k, generator=g)
     nout = max(1, int(round(k * frac)))
     cols = torch.randperm(k, generator=g)[:nout]

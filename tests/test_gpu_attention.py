@@ -40,7 +40,7 @@ def qkv(L, H, seed, k_offset=True, Lk=None):
     q = torch.randn(L, H, 128, generator=g)
     k = torch.randn(Lk, H, 128, generator=g)
     if k_offset:
-        k = k + torch.randn(1, H, 128, generator=g) * 3.0   # per-channel offset
+        k = k + torch.randn(1, H, 128, generator=g) * 3.0   # per-channel offset: the K-smoothing case
     v = torch.randn(Lk, H, 128, generator=g)
     return q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
 

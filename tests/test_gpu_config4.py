@@ -1,4 +1,4 @@
-"""BASELINE config 4 at its real length: Sparge attention over L = 219,600 tokens
+"""Sparge attention at full length: L = 219,600 tokens
 (a 61 x 45 x 80 video grid), 128 x 64 blocks (Qb 1716 x Kb 3432), top-CDF 0.6 +
 first column + diagonal.
 

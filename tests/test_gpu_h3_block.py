@@ -10,7 +10,8 @@ QKV ConvRot INT8 (per-row scales), out-proj and FC1 packed W4A8 (group 16, e4m3 
 so the comparison does not depend on block selection.
 
 The quantized path (per-token INT8, W4/W8 weights, INT8 QK / FP8 PV) is compared on the
-residual update x_out - x_in with the tolerance of the BASELINE-shaped block test.
+residual update x_out - x_in with the tolerance of the benchmark-shaped block test
+(test_gpu_block.py).
 """
 
 import math

@@ -119,7 +119,7 @@ def test_gemm_i32_bit_exact(ops, m, n, k):
 
 
 def test_gemm_i32_full_size_vs_cublas(ops):
-    """BASELINE config 1 shape 4096^3: int32 accumulators equal cuBLASLt's (torch._int_mm)."""
+    """The INT8 GEMM benchmark shape 4096^3: int32 accumulators equal cuBLASLt's (torch._int_mm)."""
     g = torch.Generator().manual_seed(0)
     a = torch.randint(-127, 128, (4096, 4096), generator=g, dtype=torch.int16).to(torch.int8).cuda()
     b = torch.randint(-127, 128, (4096, 4096), generator=g, dtype=torch.int16).to(torch.int8).cuda()

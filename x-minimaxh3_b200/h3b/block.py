@@ -37,7 +37,7 @@ class BlockConfig:
     heads: int = 32
     head_dim: int = 128
     ffn: int = 16384
-    mlp_act: str = "gelu_tanh"       # "gelu_tanh" (BASELINE) or "swiglu" (real H3: fc1 out = 2*ffn)
+    mlp_act: str = "gelu_tanh"       # "gelu_tanh" (the benchmark block) or "swiglu" (real H3: fc1 out = 2*ffn)
     w4_group: int = 128
     convrot: int = 256
     eps: float = 1e-5
@@ -134,7 +134,7 @@ class DiTBlockB200:
 
     The four projections are `h3b.quantization` layers (INT8 or packed W4A8, chosen per
     layer as the checkpoint records); `DiTBlockB200(cfg)` random-initialises them in the
-    formats BASELINE names (INT8 attention projections, W4A8 MLP) and
+    benchmark block's formats (INT8 attention projections, W4A8 MLP) and
     `h3b.checkpoint.load_block` assembles them from a checkpoint."""
 
     def __init__(self, cfg: BlockConfig, device="cuda", seed: int = 0, group=None):
