@@ -245,7 +245,8 @@ def gen_qk_rope():
         arrays.update({f"r{rot}_q": bits(q), f"r{rot}_k": bits(k), f"r{rot}_qw": bits(qw), f"r{rot}_kw": bits(kw),
                        f"r{rot}_cos": bits(table[0, :, 0, :, 0, 0].contiguous()),
                        f"r{rot}_sin": bits(table[0, :, 0, :, 1, 0].contiguous()),
-                       f"r{rot}_qo": bits(qo), f"r{rot}_ko": bits(ko)})
+                       f"r{rot}_qo": bits(qo), f"r{rot}_ko": bits(ko),
+                       f"r{rot}_angles": angles.numpy(), f"r{rot}_table": bits(table)})
         assert table.shape[3] == half
     save("qk_rope.npz", **arrays)
 

@@ -154,6 +154,20 @@ def test_rope_tables_from_both_frequency_forms(ckpt):
     assert torch.equal(c, c2) and torch.equal(s, s2)
 
 
+@pytest.mark.parametrize("rot", [128, 96])
+def test_rope_tables_equal_reference_rotation_table(rot):
+    """The cos / sin tables the kernels read, built from the engine's split-half angles and
+    from its packed table, equal the reference's rope_rotation_table entries
+    (model/layers.py:60-69) bit for bit (fixture tests/golden/qk_rope.npz)."""
+    z = np.load(os.path.join(G, "qk_rope.npz"))
+    table = torch.from_numpy(z[f"r{rot}_table"].astype(np.int16)).view(torch.bfloat16)
+    for freq in (torch.from_numpy(z[f"r{rot}_angles"]), table):
+        c, s = rope_tables_from_frequencies(freq)
+        assert c.shape == (table.shape[1], rot // 2)
+        np.testing.assert_array_equal(c.view(torch.int16).numpy().view(np.uint16), z[f"r{rot}_cos"])
+        np.testing.assert_array_equal(s.view(torch.int16).numpy().view(np.uint16), z[f"r{rot}_sin"])
+
+
 def _layer_tensors(state, name):
     p = f"{HC.PREFIX}.{name}."
     return {k[len(p):]: v for k, v in state.items() if k.startswith(p)}
