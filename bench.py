@@ -53,6 +53,13 @@ def parse():
                     "91,68,120 = 1080p/15 s); L is its product unless --tokens is given")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", type=str, default="",
+                    help="run one kernel case instead of the block (for ncu captures and CUDA-event timing); "
+                         "see KERNEL_CASES")
+    ap.add_argument("--reps", type=int, default=2, help="launches of --case")
+    ap.add_argument("--time", action="store_true", help="print the mean CUDA-event time of the --case launches")
+    ap.add_argument("--kernel-table", action="store_true",
+                    help="time every kernel of one block step alone at the bench shape (markdown table)")
     return ap.parse_args()
 
 
@@ -98,6 +105,218 @@ def run_reference(args, L):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- single-kernel cases
+
+KERNEL_CASES = """
+    attn_dense / attn_sparse   h3b_attention, L = 65,536, 8 heads (sparse: cdf 0.6 mask)
+    gemm                       h3b_int8_gemm_dequant, 16,384 x 4,096 x 4,096
+    quant_convrot              h3b_quantize_int8_rowwise_convrot, 65,536 x 4,096
+    quant_gelu                 the same with the tanh-GELU input activation, 16,384 x 16,384
+    rms_adaln                  h3b_rms_adaln_quantize_int8 (ConvRot), 65,536 x 4,096
+    pool_q                     h3b_pool_sim_quant on the queries, L = 65,536, 32 heads, 128-row blocks
+    mask                       h3b_block_mask (cdf 0.6 + first column + diagonal), L = 65,536, 32 heads
+    qk_rope                    h3b_qk_rmsnorm_rope on QKV rows [65,536, 3 x 4,096], rotary width 128
+    keys                       K mean + pool / similarity / INT8 (prepare_keys), L = 65,536, 32 heads
+    values                     V absmax + FP8 transpose (prepare_values), L = 65,536, 32 heads
+    w4_decode                  h3b_dequant_int4_grouped_to_int8, 16,384 x 4,096, G = 128
+"""
+
+
+def _kernel_case(name: str, g):
+    """Seeded inputs for one kernel at a size that keeps an `ncu --set full` capture short
+    (inputs larger than L2, a few GB on the device at most); returns the launch."""
+    import torch
+
+    from h3b import attention as A
+    from h3b import ops
+
+    dev = "cuda"
+    if name in ("attn_dense", "attn_sparse"):
+        L, H = 65536, 8
+        q, k, v = (torch.randn(L, H, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+        pk, _ = A.prepare_keys(k)
+        pq, pv = A.prepare_queries(q), A.prepare_values(v)
+        bm = (A.block_mask(pq, pk, A.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True))
+              if name == "attn_sparse" else None)
+        return lambda: A.attention(pq, pk, pv, bm)
+    if name == "gemm":
+        M, N, K = 16384, 4096, 4096
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        xs = torch.rand(M, device=dev, generator=g)
+        ws = torch.rand(N, device=dev, generator=g)
+        return lambda: ops.int8_linear_prequantized(a, xs, b, ws)
+    if name == "quant_convrot":
+        x = torch.randn(65536, 4096, device=dev, generator=g).bfloat16()
+        return lambda: ops.quantize_int8_rowwise_convrot64(x, 256)
+    if name == "quant_gelu":
+        x = torch.randn(16384, 16384, device=dev, generator=g).bfloat16()
+        return lambda: ops.quantize_int8_rowwise_convrot64(x, 256, "gelu_tanh")
+    if name == "rms_adaln":
+        x = torch.randn(65536, 4096, device=dev, generator=g).bfloat16()
+        w = (1 + 0.05 * torch.randn(4096, device=dev, generator=g)).bfloat16()
+        sc = (0.1 * torch.randn(4096, device=dev, generator=g)).bfloat16()
+        sh = (0.1 * torch.randn(4096, device=dev, generator=g)).bfloat16()
+        return lambda: ops.rms_adaln_quantize_int8(x, w, sc, sh, None, 1e-5, 256)
+    if name in ("keys", "values"):
+        x = torch.randn(65536, 32, 128, device=dev, generator=g).bfloat16()
+        return (lambda: A.prepare_keys(x)) if name == "keys" else (lambda: A.prepare_values(x))
+    if name in ("pool_q", "mask"):
+        L, H = 65536, 32
+        q, k = (torch.randn(L, H, 128, device=dev, generator=g).bfloat16() for _ in range(2))
+        if name == "pool_q":
+            return lambda: A.prepare_queries(q)
+        pq = A.prepare_queries(q)
+        pk, _ = A.prepare_keys(k)
+        cfg = A.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True)
+        return lambda: A.block_mask(pq, pk, cfg)
+    if name == "qk_rope":
+        L, H = 65536, 32
+        qkv = torch.randn(L, 3 * H * 128, device=dev, generator=g).bfloat16()
+        w = (1 + 0.05 * torch.randn(128, device=dev, generator=g)).bfloat16()
+        ang = torch.rand(L, 64, device=dev, generator=g) * 6.0
+        cos, sin = ang.cos().bfloat16(), ang.sin().bfloat16()
+        return lambda: ops.qk_rmsnorm_rope_(qkv, H, 0, H * 128, w, w, cos, sin, 1e-6)
+    if name == "w4_decode":
+        N, K, G = 16384, 4096, 128
+        qd = torch.randint(-128, 128, (N, K // 2), dtype=torch.int8, device=dev, generator=g)
+        srel = torch.rand(N, K // G, device=dev, generator=g) * 20 + 1
+        return lambda: ops.dequant_int4_grouped_to_int8(qd, srel, None, G)
+    raise SystemExit(f"unknown case {name!r}; cases:{KERNEL_CASES}")
+
+
+def run_case(args) -> int:
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    fn = _kernel_case(args.case, g)
+    if args.time:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        print(f"{args.case}: {s.elapsed_time(e) / args.reps:.3f} ms per launch")
+    else:
+        for _ in range(args.reps):
+            fn()
+        torch.cuda.synchronize()
+        print(f"{args.case}: ok")
+    return 0
+
+
+def _timed(fn, reps: int) -> float:
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def run_kernel_table(args, L) -> int:
+    """Every kernel of one block step at the bench shape, each call timed alone with CUDA
+    events over --reps launches after warm-up on inputs larger than L2, against its roofline:
+    bytes that must cross HBM once (read + write) for the memory-bound kernels, 2 x
+    multiply-adds for the tensor-core ones (the attention counts the tiles the bitmap keeps;
+    fp32 multiply-adds for the mask's scores).  Peaks: HBM copy bandwidth, and twice the
+    burst bf16 GEMM rate for INT8/FP8, from MEASURED_PEAKS.json (fallback figures if absent)."""
+    import torch
+
+    from h3b import attention as A
+    from h3b import block as B
+    from h3b import ops
+
+    pk_, src = measured_peaks()
+    hbm, tensor = float(pk_["hbm_gbs"]), 2.0 * float(pk_["bf16_tflops"])
+    reps = max(args.reps, 3)
+    cfg = B.BlockConfig()
+    blk = B.DiTBlockB200(cfg, device="cuda", seed=0)
+    D, F, H = cfg.hidden, cfg.ffn, cfg.heads
+    W = H * cfg.head_dim
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(L, D, device="cuda", generator=g).to(torch.bfloat16)
+    t = torch.randn(cfg.t_dim, device="cuda", generator=g).to(torch.bfloat16)
+    rope = B.rope_tables(args.grid_t, cfg.rope_splits, device="cuda")
+    mod = blk.modulation(t)
+    sh_a, sc_a, ga, sh_m, sc_m, gm = mod.unbind(1)
+    rows = []
+
+    def row(name, ms, work, kind):
+        if kind == "hbm":
+            achieved = work / ms / 1e6
+            rows.append((name, ms, f"{work / 1e9:.2f} GB", f"{achieved:,.0f} GB/s", achieved / hbm))
+        elif kind == "fma":
+            rows.append((name, ms, f"{work / 1e9:.1f} GFLOP", f"{work / ms / 1e9:,.1f} TFLOP/s fp32", None))
+        else:
+            achieved = work / ms / 1e9
+            rows.append((name, ms, f"{work / 1e12:.1f} Tops", f"{achieved:,.0f} TOPS", achieved / tensor))
+
+    ms = _timed(lambda: ops.rms_adaln_quantize_int8(x, blk.norm1, sc_a, sh_a, None, cfg.eps, 256), reps)
+    row("rms_adaln + ConvRot INT8 quantizer (K 4096) x2", ms, L * D * 3 + L * 4, "hbm")
+    xq, xs = ops.rms_adaln_quantize_int8(x, blk.norm1, sc_a, sh_a, None, cfg.eps, 256)
+    qkv = torch.empty(L, 3 * W, device="cuda", dtype=torch.bfloat16)
+    ms = _timed(lambda: blk.qkv.forward_prequantized_qk_rope(xq, xs, qkv, H, 0, W, blk.q_norm, blk.k_norm, rope[0],
+                                                             rope[1], cfg.qk_eps), reps)
+    row("QKV INT8 GEMM + dequant + q/k RMSNorm/RoPE epilogue (N 12288, K 4096)", ms, 2.0 * L * 3 * W * D, "tensor")
+    view = qkv.view(L, 3, H, cfg.head_dim)
+    q, k, v = view[:, 0], view[:, 1], view[:, 2]
+    ms = _timed(lambda: A.prepare_values(v), reps)
+    row("V -> FP8 (absmax, scale, transpose)", ms, L * W * 2 + L * W, "hbm")
+    ms = _timed(lambda: A.prepare_keys(k), reps)
+    row("K mean + pool / similarity / INT8", ms, 2 * L * W * 2 + L * W, "hbm")
+    ms = _timed(lambda: A.prepare_queries(q), reps)
+    row("Q pool / similarity / INT8", ms, L * W * 2 + L * W, "hbm")
+    pv = A.prepare_values(v)
+    pk, _ = A.prepare_keys(k)
+    pq = A.prepare_queries(q)
+    ms = _timed(lambda: A.block_mask(pq, pk, cfg.mask), reps)
+    qb, kb = math.ceil(L / 128), math.ceil(L / 64)
+    row("Sparge block mask (fp32 scores + selection)", ms, 2.0 * qb * kb * H * 128, "fma")
+    bitmap = A.block_mask(pq, pk, cfg.mask)
+    ms = _timed(lambda: A.attention(pq, pk, pv, bitmap), reps)
+    row(f"attention (INT8 QK, FP8 PV; kept tiles {B.kept_tiles(bitmap, L) / (qb * kb * H):.3f})", ms,
+        B.attention_ops(bitmap, L, L, H), "tensor")
+    o2 = A.attention(pq, pk, pv, bitmap).view(L, W)
+    ms = _timed(lambda: blk.out.quantize(o2), reps)
+    row("ConvRot INT8 quantizer (out-proj input, K 4096)", ms, L * W * 3 + L * 4, "hbm")
+    oq, os_ = blk.out.quantize(o2)
+    xr = x.clone()
+    ms = _timed(lambda: blk.out.gated_residual_(xr, ga[0], oq, os_), reps)
+    row("out-proj INT8 GEMM + gated residual (N 4096, K 4096)", ms, 2.0 * L * D * W, "tensor")
+    ms = _timed(lambda: blk.fc1.int8_weight(), reps)
+    row("W4 -> INT8 decode, FC1 weight (16384 x 4096)", ms, F * D / 2 + F * (D // cfg.w4_group) * 4 + F * D, "hbm")
+    xq2, xs2 = ops.rms_adaln_quantize_int8(x, blk.norm2, sc_m, sh_m, None, cfg.eps, 256)
+    ms = _timed(lambda: blk.fc1.forward_prequantized(xq2, xs2), reps)
+    row("FC1 W4A8 (decode + INT8 GEMM, N 16384, K 4096)", ms, 2.0 * L * F * D, "tensor")
+    h = blk.fc1.forward_prequantized(xq2, xs2)
+    ms = _timed(lambda: blk.fc2.quantize(h, cfg.mlp_act), reps)
+    row("tanh-GELU + ConvRot INT8 quantizer (K 16384)", ms, L * F * 3 + L * 4, "hbm")
+    hq, hs = blk.fc2.quantize(h, cfg.mlp_act)
+    del h
+    ms = _timed(lambda: blk.fc2.gated_residual_(xr, gm[0], hq, hs), reps)
+    row("FC2 W4A8 + gated residual (N 4096, K 16384)", ms, 2.0 * L * D * F, "tensor")
+    step = _timed(lambda: blk.forward(x.clone(), t, rope), 3)
+    print(f"L = {L}, {torch.cuda.get_device_name()}; peaks ({src}): HBM {hbm:,.0f} GB/s, "
+          f"INT8/FP8 {tensor:,.0f} TOPS (2 x bf16 burst)\n")
+    print("| kernel (one call) | ms | work | achieved | of peak |")
+    print("|---|---:|---:|---:|---:|")
+    for name, ms, work, ach, frac in rows:
+        print(f"| {name} | {ms:.3f} | {work} | {ach} | {'-' if frac is None else f'{frac:.2f}'} |")
+    print(f"\nblock forward (all of the above, norm quantizer twice, x.clone() included): {step:.2f} ms")
     return 0
 
 
@@ -350,6 +569,10 @@ def main():
     if len(args.grid_t) != 3 or min(args.grid_t) <= 0:
         raise SystemExit("--grid takes three positive integers T,H,W")
     L = args.tokens or args.grid_t[0] * args.grid_t[1] * args.grid_t[2]
+    if args.case:
+        return run_case(args)
+    if args.kernel_table:
+        return run_kernel_table(args, L)
     if args.impl == "reference":
         return run_reference(args, L)
     return run_h3b(args, L)

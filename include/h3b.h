@@ -174,10 +174,22 @@ int h3b_key_mean_no_alloc(const void* k, int64_t L, int64_t H, int64_t k_row_str
  *   scale   f32  [H, nb]       = max|value| / 127 + 1e-7
  * x: bf16 NHD [L, H*128] rows of stride x_row_stride; nb = ceil(L/block),
  * Lpad >= nb*block (rows beyond nb*block are not written); thr: f32 [H].
+ * block 32 gives the per-warp Q groups of Sage's per_warp granularity (32-row
+ * groups; model/kernels.py:5571-5573), whose pooled / similar outputs go unused.
  * Replaces pool_sim_quant_nhd (model/sparge_nhd.py:51-227). */
 int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride, const void* mean,
                        int block, const void* thr, void* pooled, void* similar, void* qi8, void* scale,
                        int64_t Lpad, void* stream);
+
+/* h3b_pool_sim_quant over one slab of `rows` tokens of a longer sequence, writing
+ * into that sequence's arrays: pooled / similar / scale point at the slab's first
+ * block of head 0 with `blocks_per_head` blocks between heads, qi8 at the slab's
+ * first row of head 0 with `Lpad` rows between heads.  The slab starts on a block
+ * boundary.  Replaces the per-slab get_pool_sim_triton_simmean_fuse_quant of the
+ * compact K/V builder (model/kernels.py:2733-2751). */
+int h3b_pool_sim_quant_slab(const void* x, int64_t rows, int64_t H, int64_t x_row_stride, const void* mean,
+                            int block, const void* thr, void* pooled, void* similar, void* qi8, void* scale,
+                            int64_t blocks_per_head, int64_t Lpad, void* stream);
 
 /* Per-head RMSNorm (weight, eps) of Q and K followed by split-half partial
  * RoPE over the first rot_dim channels, in place on bf16 projection rows:
@@ -200,6 +212,17 @@ int h3b_qk_rmsnorm_rope(void* qkv, int64_t L, int64_t H, int64_t row_stride, int
 int h3b_value_fp8(const void* v, int64_t L, int64_t H, int64_t v_row_stride, int64_t Lpad, void* vt,
                   void* vscale, void* stream);
 
+/* V -> FP8 E4M3 for one slab of `rows` tokens with a per-(head, channel) absmax
+ * the caller gathered over the whole sequence beforehand: codes of v * (2.25 /
+ * absmax) written transposed at vt (the slab's first token column of head 0,
+ * channel 0; `vt_row_pitch` bytes between channel rows), in ceil(rows/128)
+ * 128-token tiles (tokens past `rows` in the last tile are zero); vscale (f32
+ * [H, 128], may be NULL) receives max(absmax / 2.25, 1e-12).  absmax: f32 [H, 128].
+ * Replaces _write_compact_value_fp8 / write_sage_fp8_slab (model/kernels.py:
+ * 2491-2526, model/compact_fp8.py:205-300). */
+int h3b_value_fp8_given_absmax(const void* v, int64_t rows, int64_t H, int64_t v_row_stride, const void* absmax,
+                               void* vt, int64_t vt_row_pitch, void* vscale, void* stream);
+
 /* ---------------------------------------------------------------- block-sparse mask */
 
 /* Parameters of the block-sparse selector (model/kernels.py:3668-3941). */
@@ -214,6 +237,13 @@ typedef struct h3b_mask_params {
   int temporal_radius;          /* < 0 off; else the temporal correspondence rail */
   int temporal_spatial_radius;
   int64_t frames, frame_tokens, protected_tokens, query_tokens;
+  /* device memory, int64 [query_tokens], or NULL: the position in the video of
+     each query row of a chunk of selected queries (model/kernels.py:5247-5254);
+     the rail then takes query block i's centre from entry min(128 i + 64,
+     query_tokens - 1).  NULL: the queries are the whole video in order. */
+  const int64_t* query_indices;
+  int64_t protected_query_blocks; /* first query blocks kept dense over every key
+                                     (model/kernels.py:2423-2426) */
 } h3b_mask_params;
 
 /* Pooled scores softmax(bf16(pq . pk) * 128^-0.5, non-similar K -> -inf) per
@@ -237,7 +267,7 @@ int h3b_bitmap_to_lut(const void* bitmap, int64_t rows, int64_t Kb, void* lut, v
  * online softmax, P and V in FP8 E4M3 (tcgen05 kind::f8f6f4), fp32 output
  * accumulation.  Visits only the K blocks whose bit is set in `bitmap`
  * ([H, ceil(Lq/128), ceil(Kb/32)] words) or all of them when bitmap is NULL.
- * q: int8 [H, Lqpad, 128], q_scale f32 [H, ceil(Lq/q_block)] (q_block 64 or 128);
+ * q: int8 [H, Lqpad, 128], q_scale f32 [H, ceil(Lq/q_block)] (q_block 32, 64 or 128);
  * k: int8 [H, Lkpad, 128], k_scale f32 [H, ceil(Lk/64)];
  * vt: e4m3 [H, 128, Lkpad], v_scale f32 [H, 128];
  * out: bf16 NHD rows [Lq, H*128] with row stride out_row_stride.

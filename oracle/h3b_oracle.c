@@ -630,13 +630,17 @@ static int cmp_desc_idx(const void* a, const void* b) {
  *   `protected_kb` columns; optional (flags bit0) column 0, (bit1) the diagonal
  *   K blocks covering the Q block's rows; (temporal_radius >= 0) the temporal
  *   correspondence rail of kernels.py:5206-5294 for an (frames x frame_tokens)
- *   video that starts after `protected_tokens` prefix keys.
+ *   video that starts after `protected_tokens` prefix keys; with `q_index`
+ *   (a chunk of selected queries, kernels.py:5247-5254) query block i's centre
+ *   is q_index[min(128 i + 64, q_tokens - 1)], else that row number itself;
+ *   the first `protected_qb` query blocks keep every key block
+ *   (kernels.py:2423-2426).
  * Output: bitmap words [H, Qb, ceil(Kb/32)], bit j%32 of word j/32. */
 void h3bo_block_mask(const uint16_t* pooled_q, const uint8_t* simq, int64_t Qb, const uint16_t* pooled_k,
                      const uint8_t* simk, int64_t Kb, int64_t H, int mode, const float* budget,
                      int64_t protected_kb, int flags, int temporal_radius, int temporal_spatial_radius,
                      int64_t frames, int64_t frame_tokens, int64_t protected_tokens, int64_t q_tokens,
-                     uint32_t* bitmap) {
+                     const int64_t* q_index, int64_t protected_qb, uint32_t* bitmap) {
     int64_t words = (Kb + 31) / 32;
     uint16_t* p = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)Kb);
     uint32_t* keys = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)Kb);
@@ -669,12 +673,13 @@ void h3bo_block_mask(const uint16_t* pooled_q, const uint8_t* simq, int64_t Qb, 
                 }
             }
             for (int64_t j = 0; j < Kb; ++j) {
-                int on = !simk[h * Kb + j] || !simq[h * Qb + i] || j < protected_kb;
+                int on = !simk[h * Kb + j] || !simq[h * Qb + i] || j < protected_kb || i < protected_qb;
                 if ((flags & 1) && j == 0) on = 1;
                 if ((flags & 2) && (j == 2 * i || j == 2 * i + 1)) on = 1;
                 if (temporal_radius >= 0 && frame_tokens > 0) {
                     int64_t video = frames * frame_tokens;
                     int64_t qc = i * 128 + 64; if (qc > q_tokens - 1) qc = q_tokens - 1;
+                    if (q_index) qc = q_index[qc];
                     int64_t qf = qc / frame_tokens, qs = qc % frame_tokens;
                     int64_t kc = j * 64 + 32 - protected_tokens;
                     int valid = kc >= 0 && kc < video;

@@ -242,7 +242,7 @@ def value_fp8(v_bf16, Lpad=None):
 
 def block_mask(pooled_q, simq, pooled_k, simk, *, mode, budget, protected_kb=0, flags=0,
                temporal_radius=-1, temporal_spatial_radius=0, frames=0, frame_tokens=0,
-               protected_tokens=0, q_tokens=0):
+               protected_tokens=0, q_tokens=0, q_index=None, protected_qb=0):
     pq = _c(pooled_q, np.uint16)
     pk = _c(pooled_k, np.uint16)
     H, Qb, _ = pq.shape
@@ -253,7 +253,8 @@ def block_mask(pooled_q, simq, pooled_k, simk, *, mode, budget, protected_kb=0, 
     lib().h3bo_block_mask(_p(pq), _p(_c(simq, np.uint8)), I64(Qb), _p(pk), _p(_c(simk, np.uint8)), I64(Kb),
                           I64(H), ctypes.c_int(mode), _p(bud), I64(protected_kb), ctypes.c_int(flags),
                           ctypes.c_int(temporal_radius), ctypes.c_int(temporal_spatial_radius), I64(frames),
-                          I64(frame_tokens), I64(protected_tokens), I64(q_tokens), _p(bm))
+                          I64(frame_tokens), I64(protected_tokens), I64(q_tokens), _p(_c(q_index, np.int64)),
+                          I64(protected_qb), _p(bm))
     return bm
 
 

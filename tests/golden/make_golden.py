@@ -45,7 +45,9 @@ import types
 
 import numpy as np
 
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT", "")
+if not REF or not os.path.isdir(REF):
+    raise SystemExit("usage: make_golden.py <X-MinimaxH3 checkout> (or set REFERENCE_ROOT)")
 os.environ["TRITON_INTERPRET"] = "1"
 sys.path[:0] = [os.path.join(REF, "backends/turbo/vendor"), REF]
 

@@ -272,20 +272,92 @@ def test_no_device_timeouts_recorded(attn):
 
 def test_long_sequence_protocol_matches_whole_sequence(attn):
     """Prepared K/V + query chunks reproduce the one-shot backend (same kernels,
-    same blocks) -- the streamed protocol of model/layers.py:341-356."""
+    same blocks) -- the streamed protocol of model/layers.py:341-356, with the
+    prepared-V tuple the reference caller unpacks (model/layers.py:668-680)."""
     q, k, v = qkv(1024 + 256, 2, seed=17)
     qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
     backend = attn.SpargeLongSequenceB200(attn.MaskConfig("topk", 0.5))
-    vt, vs, L, Lpad, H = backend.prepare_long_sequence_values(vc)
-    prepared = backend.prepare_long_sequence_keys(kc, vt, vs)
-    whole = backend.long_sequence_all_queries(qc, prepared)
+    vt, vs, heads, key_tokens, head_dim = backend.prepare_long_sequence_values(vc.unsqueeze(0))
+    assert (heads, key_tokens, head_dim) == (2, 1280, 128)
+    assert vt.shape == (1, 2, 128, 1280) and vt.dtype == torch.float8_e4m3fn and vs.shape == (1, 2, 128)
+    prepared = backend.prepare_long_sequence_keys(kc.unsqueeze(0), vt, vs)
+    whole = backend.long_sequence_video_queries(qc, prepared, protected_tokens=0, query_token_indices=None)
     one_shot = attn.SpargeAttentionB200(attn.MaskConfig("topk", 0.5))(qc, kc, vc)
     assert torch.equal(whole, one_shot)
     # a 128-aligned chunk sees the same pooled query blocks -> same rows
     chunk = backend.long_sequence_video_queries(qc[512:1024], prepared, protected_tokens=0,
                                                 query_token_indices=torch.arange(512, 1024, device="cuda"))
     assert torch.equal(chunk, whole[512:1024])
+    with pytest.raises(ValueError):
+        backend.prepare_long_sequence_keys(kc[:1000].unsqueeze(0), vt, vs)
     dense = attn.DenseLongSequenceB200()
-    prep_d = dense.prepare_long_sequence_keys(kc, vt, vs)
+    prep_d = dense.prepare_long_sequence_keys(kc.unsqueeze(0), vt, vs)
     assert torch.equal(dense.long_sequence_prefix_queries(qc[:256], prep_d),
-                       attn.SageAttentionB200()(qc, kc, vc)[:256])
+                       attn.SageAttentionB200(q_block=32)(qc, kc, vc)[:256])
+    assert torch.equal(dense.long_sequence_all_queries(qc, prep_d), attn.SageAttentionB200(q_block=32)(qc, kc, vc))
+
+
+@pytest.mark.parametrize("selected", ["offset", "gathered"])
+def test_block_mask_query_indices_and_protected_rows_bit_exact(attn, selected):
+    """Temporal rail centred through a chunk's token indices (model/kernels.py:5247-5254)
+    and protected query rows (kernels.py:2423-2426): bit-exact vs the oracle."""
+    g = torch.Generator().manual_seed(5)
+    frames, ftok, prefix = 6, 300, 192
+    Lk = prefix + frames * ftok
+    q = torch.randn(640, 3, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(Lk, 3, 128, generator=g).to(torch.bfloat16)
+    pq = attn.prepare_queries(q.cuda())
+    pk, _ = attn.prepare_keys(k.cuda())
+    if selected == "offset":
+        idx = torch.arange(900, 900 + 640)
+    else:  # calibration-style: whole 128-row blocks gathered from across the video
+        starts = torch.tensor([0, 1280, 384, 1536, 768])
+        idx = (starts[:, None] + torch.arange(128)[None, :]).reshape(-1)
+    mc = attn.MaskConfig("topk", 0.2, protected_tokens=prefix, temporal_radius=1, temporal_spatial_radius=1,
+                         video_layout=(frames, ftok))
+    bm = attn.block_mask(pq, pk, mc, query_indices=idx.cuda(), protected_query_tokens=130)
+    ref = O.block_mask(bits(pq.pooled), pq.similar.cpu().numpy(), bits(pk.pooled), pk.similar.cpu().numpy(),
+                       mode=0, budget=0.2, protected_kb=(prefix + 63) // 64, flags=0, temporal_radius=1,
+                       temporal_spatial_radius=1, frames=frames, frame_tokens=ftok, protected_tokens=prefix,
+                       q_tokens=640, q_index=idx.numpy(), protected_qb=2)
+    np.testing.assert_array_equal(bm.cpu().numpy().view(np.uint32), ref)
+    no_idx = attn.block_mask(pq, pk, mc, protected_query_tokens=130)
+    assert not torch.equal(no_idx, bm), "the indices should move the rail"
+
+
+def test_compact_kv_builder_matches_whole_build(attn):
+    """Slab-by-slab K/V (begin_compact_long_sequence_kv, model/kernels.py:2677-2772) equals
+    the whole-sequence preparation byte for byte when given the same K mean and V absmax."""
+    L, H = 1000, 3
+    _, k, v = qkv(L, H, seed=41)
+    kc, vc = k.cuda(), v.cuda()
+    pk, mean = attn.prepare_keys(kc)
+    pv = attn.prepare_values(vc)
+    absmax = vc.float().abs().amax(0)
+    backend = attn.SpargeLongSequenceB200()
+    b = backend.begin_compact_long_sequence_kv(key_tokens=L, heads=H, head_dim=128, key_mean=mean.float(),
+                                               value_absmax=absmax, device=kc.device)
+    for s0 in range(0, L, 256):
+        b.add(s0, kc[s0:s0 + 256], vc[s0:s0 + 256])
+    prep = b.finish()
+    for a_, b_ in ((prep.keys.qi8, pk.qi8), (prep.keys.scale, pk.scale), (prep.keys.pooled, pk.pooled),
+                   (prep.keys.similar, pk.similar), (prep.values.vt, pv.vt), (prep.values.scale, pv.scale)):
+        assert a_.shape == b_.shape
+        assert torch.equal(a_.view(torch.uint8) if a_.dtype != torch.uint8 else a_,
+                           b_.view(torch.uint8) if b_.dtype != torch.uint8 else b_)
+    with pytest.raises(ValueError):
+        b2 = backend.begin_compact_long_sequence_kv(key_tokens=L, heads=H, head_dim=128, key_mean=mean.float(),
+                                                    value_absmax=absmax, device=kc.device)
+        b2.add(64, kc[64:128], vc[64:128])
+
+
+def test_dense_attention_per_warp_q(attn):
+    """Per-warp (32-row) Q scales, Sage's per_warp granularity (model/kernels.py:5571-5573)."""
+    q, k, v = qkv(700, 2, seed=6)
+    pv = attn.prepare_values(v.cuda())
+    pk, _ = attn.prepare_keys(k.cuda())
+    pq = attn.prepare_queries(q.cuda(), block=32)
+    assert pq.scale.shape == (2, 22)
+    out = attn.attention(pq, pk, pv).float().cpu()
+    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv))
+    assert cosine(out, ref) >= 0.999 and rel_l2(out, ref) <= 3e-2

@@ -5,9 +5,11 @@
 // (model/kernels.py:3668-3941): scores = bf16(pooled_q . pooled_k) * 128^-0.5,
 // non-similar K blocks -> -inf, softmax, keep the `count` most probable K blocks
 // (fixed Top-K, kernels.py:3206-3253) or the top-CDF prefix (SpargeAttn rule),
-// then keep every non-similar K column and Q row, the protected prefix, and the
-// optional first-column / diagonal / temporal-correspondence rails
-// (kernels.py:5206-5294).
+// then keep every non-similar K column and Q row, the protected prefix (key
+// columns, and optionally whole query rows), and the optional first-column /
+// diagonal / temporal-correspondence rails (kernels.py:5206-5294; for a chunk of
+// selected video queries the rail takes each query block's centre from the
+// chunk's token indices, kernels.py:5247-5254).
 //
 // Per CTA: one head, up to 8 query blocks (one warp each).  All threads first
 // compute the 8 x Kb score matrix into shared memory (each thread one K block,
@@ -310,12 +312,14 @@ __global__ void __launch_bounds__(kMaskThreads) block_mask_kernel(MaskArgs a) {
         // probabilities are non-negative: bf16 bit patterns order like the values
         on = key > T;
         is_eq = key == T;
-        on |= !simk[j] || !simq || j < a.protected_kb;
+        on |= !simk[j] || !simq || j < a.protected_kb || qi < a.protected_qb;
         on |= a.first_col && j == 0;
         on |= a.diag && (j == 2 * qi || j == 2 * qi + 1);
         if (a.temporal_radius >= 0 && a.frame_tokens > 0) {
           int64_t qc = qi * 128 + 64;
           if (qc > a.query_tokens - 1) qc = a.query_tokens - 1;
+          // selected queries: the block centre's position in the video
+          if (a.q_index) qc = a.q_index[qc];
           const int64_t qf = qc / a.frame_tokens, qs = qc % a.frame_tokens;
           const int64_t kc = (int64_t)j * 64 + 32 - a.protected_tokens;
           const bool valid = kc >= 0 && kc < video;

@@ -9,7 +9,9 @@
 //               NHD input with any row stride (reads Q/K straight out of the
 //               fused QKV projection output)
 //  value fp8    per-(head, channel) absmax, V * 2.25/absmax -> E4M3, transposed
-//               to [H, 128, Lpad] (model/compact_fp8.py:13-300)
+//               to [H, 128, Lpad] (model/compact_fp8.py:13-300); also slab by
+//               slab with an absmax the caller gathered beforehand (the compact
+//               K/V build of model/kernels.py:2491-2526, 2677-2772)
 // Every reduction runs in the order the CPU oracle restates, so results are
 // bit-identical to it.
 #include <mutex>
@@ -149,7 +151,7 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r0 = (int64_t)b * a.blk;
   const int valid = (int)((a.L - r0) < a.blk ? (a.L - r0) : a.blk);
-  const int nb = (int)((a.L + a.blk - 1) / a.blk);
+  const int64_t nbs = a.nb_stride ? a.nb_stride : (a.L + a.blk - 1) / a.blk;
 
   float mean4[4] = {0.f, 0.f, 0.f, 0.f};
   if (a.mean) {
@@ -206,15 +208,15 @@ __global__ void __launch_bounds__(128) pool_sim_quant_kernel(PoolArgs a) {
       pooled[i] = f32_to_bf16_bits(__fdiv_rn(ps, (float)valid));
       s2[i] = __fmul_rn(ss, ss);
     }
-    *reinterpret_cast<uint2*>(a.pooled + ((int64_t)h * nb + b) * kD + 4 * lane) =
+    *reinterpret_cast<uint2*>(a.pooled + ((int64_t)h * nbs + b) * kD + 4 * lane) =
         make_uint2((uint32_t)pooled[0] | ((uint32_t)pooled[1] << 16), (uint32_t)pooled[2] | ((uint32_t)pooled[3] << 16));
     const float g = warp_butterfly_sum(__fadd_rn(__fadd_rn(__fadd_rn(s2[0], s2[1]), s2[2]), s2[3]));
     const float simv = __fdiv_rn(g, (float)(valid * valid));
     const float am = fmaxf(fmaxf(amax_s[0], amax_s[1]), fmaxf(amax_s[2], amax_s[3]));
     const float sc = __fadd_rn(__fdiv_rn(am, 127.0f), 1e-7f);
     if (lane == 0) {
-      a.similar[(int64_t)h * nb + b] = (uint8_t)(valid == a.blk && simv > a.thr[h]);
-      a.scale[(int64_t)h * nb + b] = sc;
+      a.similar[(int64_t)h * nbs + b] = (uint8_t)(valid == a.blk && simv > a.thr[h]);
+      a.scale[(int64_t)h * nbs + b] = sc;
       scale_s = sc;
     }
   }
@@ -374,9 +376,11 @@ __global__ void __launch_bounds__(256) value_absmax_kernel(const uint16_t* __res
 
 // One CTA per (128-token tile, head): read V[128 tokens][128 ch] (bf16) into
 // shared memory, write vt[h][ch][tile] as E4M3, 128 bytes per channel row.
+// vscale (optional): max(amax / 2.25, 1e-12), written by the first tile's CTAs.
 __global__ void __launch_bounds__(256) value_fp8_kernel(const uint16_t* __restrict__ v, int64_t L, int H,
                                                          int64_t stride, int64_t Lpad,
-                                                         const float* __restrict__ amax, uint8_t* __restrict__ vt) {
+                                                         const float* __restrict__ amax, uint8_t* __restrict__ vt,
+                                                         float* __restrict__ vscale) {
   __shared__ uint16_t tile[128][kD + 2];
   __shared__ float mul_s[kD];
   const int h = blockIdx.y;
@@ -395,6 +399,7 @@ __global__ void __launch_bounds__(256) value_fp8_kernel(const uint16_t* __restri
   if (threadIdx.x < kD) {
     const float am = amax[h * kD + threadIdx.x];
     mul_s[threadIdx.x] = am > 0.f ? __fdiv_rn(2.25f, am) : 0.f;
+    if (vscale && blockIdx.x == 0) vscale[h * kD + threadIdx.x] = fmaxf(__fdiv_rn(am, 2.25f), 1e-12f);
   }
   __syncthreads();
   // thread -> (channel, half of the 128 tokens): 64 bytes out
@@ -433,8 +438,16 @@ cudaError_t launch_value_fp8(const void* v, int64_t L, int64_t H, int64_t stride
                                          static_cast<unsigned int*>(vscale));
   dim3 g2((unsigned)(Lpad / 128), (unsigned)H);
   value_fp8_kernel<<<g2, 256, 0, s>>>(static_cast<const uint16_t*>(v), L, (int)H, stride, Lpad,
-                                      static_cast<const float*>(vscale), static_cast<uint8_t*>(vt));
+                                      static_cast<const float*>(vscale), static_cast<uint8_t*>(vt), nullptr);
   value_scale_final_kernel<<<(cols + 255) / 256, 256, 0, s>>>(static_cast<float*>(vscale), cols);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_value_fp8_given_absmax(const void* v, int64_t rows, int64_t H, int64_t stride, int64_t Lpad,
+                                          const float* absmax, void* vt, float* vscale, cudaStream_t s) {
+  dim3 g((unsigned)((rows + 127) / 128), (unsigned)H);
+  value_fp8_kernel<<<g, 256, 0, s>>>(static_cast<const uint16_t*>(v), rows, (int)H, stride, Lpad, absmax,
+                                     static_cast<uint8_t*>(vt), vscale);
   return cudaGetLastError();
 }
 

@@ -242,15 +242,33 @@ int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride
                        void* stream) {
   if (L <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "L and H must be positive");
   if (!x || !thr || !pooled || !similar || !qi8 || !scale) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
-  if (block != 64 && block != 128) return fail(H3B_ERR_UNSUPPORTED, "block must be 64 or 128");
+  if (block != 32 && block != 64 && block != 128) return fail(H3B_ERR_UNSUPPORTED, "block must be 32, 64 or 128");
   const int64_t nb = (L + block - 1) / block;
   if (Lpad < nb * block) return fail(H3B_ERR_INVALID_ARGUMENT, "Lpad < ceil(L/block)*block");
   if (x_row_stride < H * 128 || x_row_stride % 4) return fail(H3B_ERR_INVALID_ARGUMENT, "bad x_row_stride");
   if (nb > INT_MAX || H > 65535) return fail(H3B_ERR_UNSUPPORTED, "too many blocks or heads");
   h3b::PoolArgs a{static_cast<const uint16_t*>(x), L, x_row_stride, Lpad, (int)H, block,
                   static_cast<const uint16_t*>(mean), static_cast<const float*>(thr), static_cast<uint16_t*>(pooled),
-                  static_cast<uint8_t*>(similar), static_cast<int8_t*>(qi8), static_cast<float*>(scale)};
+                  static_cast<uint8_t*>(similar), static_cast<int8_t*>(qi8), static_cast<float*>(scale), 0};
   return cuda_status(h3b::launch_pool_sim_quant(a, st(stream)), "pool_sim_quant");
+}
+
+int h3b_pool_sim_quant_slab(const void* x, int64_t rows, int64_t H, int64_t x_row_stride, const void* mean, int block,
+                            const void* thr, void* pooled, void* similar, void* qi8, void* scale,
+                            int64_t blocks_per_head, int64_t Lpad, void* stream) {
+  if (rows <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "rows and H must be positive");
+  if (!x || !thr || !pooled || !similar || !qi8 || !scale) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (block != 64 && block != 128) return fail(H3B_ERR_UNSUPPORTED, "block must be 64 or 128");
+  const int64_t nb = (rows + block - 1) / block;
+  if (blocks_per_head < nb) return fail(H3B_ERR_INVALID_ARGUMENT, "blocks_per_head < ceil(rows/block)");
+  if (Lpad < nb * block) return fail(H3B_ERR_INVALID_ARGUMENT, "Lpad < ceil(rows/block)*block");
+  if (x_row_stride < H * 128 || x_row_stride % 4) return fail(H3B_ERR_INVALID_ARGUMENT, "bad x_row_stride");
+  if (nb > INT_MAX || H > 65535) return fail(H3B_ERR_UNSUPPORTED, "too many blocks or heads");
+  h3b::PoolArgs a{static_cast<const uint16_t*>(x), rows, x_row_stride, Lpad, (int)H, block,
+                  static_cast<const uint16_t*>(mean), static_cast<const float*>(thr), static_cast<uint16_t*>(pooled),
+                  static_cast<uint8_t*>(similar), static_cast<int8_t*>(qi8), static_cast<float*>(scale),
+                  blocks_per_head};
+  return cuda_status(h3b::launch_pool_sim_quant(a, st(stream)), "pool_sim_quant_slab");
 }
 
 int h3b_qk_rmsnorm_rope(void* qkv, int64_t L, int64_t H, int64_t row_stride, int64_t q_offset, int64_t k_offset,
@@ -279,6 +297,20 @@ int h3b_value_fp8(const void* v, int64_t L, int64_t H, int64_t v_row_stride, int
   return cuda_status(h3b::launch_value_fp8(v, L, H, v_row_stride, Lpad, vt, vscale, st(stream)), "value_fp8");
 }
 
+int h3b_value_fp8_given_absmax(const void* v, int64_t rows, int64_t H, int64_t v_row_stride, const void* absmax,
+                               void* vt, int64_t vt_row_pitch, void* vscale, void* stream) {
+  if (rows <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "rows and H must be positive");
+  if (!v || !absmax || !vt) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (vt_row_pitch < (rows + 127) / 128 * 128 || vt_row_pitch % 16)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "vt_row_pitch must cover ceil(rows/128)*128 tokens, a multiple of 16");
+  if (v_row_stride < H * 128 || v_row_stride % 8) return fail(H3B_ERR_INVALID_ARGUMENT, "bad v_row_stride");
+  if (!aligned16(v) || !aligned16(vt)) return fail(H3B_ERR_UNSUPPORTED, "v and vt must be 16-byte aligned");
+  return cuda_status(h3b::launch_value_fp8_given_absmax(v, rows, H, v_row_stride, vt_row_pitch,
+                                                        static_cast<const float*>(absmax), vt,
+                                                        static_cast<float*>(vscale), st(stream)),
+                     "value_fp8_given_absmax");
+}
+
 int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, const void* pooled_k,
                    const void* similar_k, int64_t Kb, int64_t H, const h3b_mask_params* p, void* bitmap,
                    void* stream) {
@@ -291,7 +323,11 @@ int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, cons
                   static_cast<const uint16_t*>(pooled_k), static_cast<const uint8_t*>(similar_k), Qb, Kb, p->mode,
                   p->budget, p->protected_key_blocks, p->keep_first_column, p->keep_diagonal, p->temporal_radius,
                   p->temporal_spatial_radius, p->frames, p->frame_tokens, p->protected_tokens, p->query_tokens,
-                  static_cast<uint32_t*>(bitmap)};
+                  static_cast<uint32_t*>(bitmap), p->query_indices, p->protected_query_blocks};
+  if (p->temporal_radius >= 0 && p->frame_tokens > 0 && p->query_tokens < 1)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "the temporal rail needs query_tokens >= 1");
+  if (p->protected_query_blocks < 0 || p->protected_key_blocks < 0)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "protected block counts must be non-negative");
   return cuda_status(h3b::launch_block_mask(a, H, st(stream)), "block_mask");
 }
 
@@ -308,7 +344,8 @@ int h3b_attention(const void* q, const void* q_scale, int q_block, int64_t Lq, i
   if (Lq == 0) return ok();
   if (!q || !q_scale || !k || !k_scale || !vt || !v_scale || !out) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
   if (Lq < 0 || Lk <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "bad sizes");
-  if (q_block != 64 && q_block != 128) return fail(H3B_ERR_UNSUPPORTED, "q_block must be 64 or 128");
+  if (q_block != 32 && q_block != 64 && q_block != 128)
+    return fail(H3B_ERR_UNSUPPORTED, "q_block must be 32, 64 or 128");
   if (Lqpad % 128 || Lqpad < Lq || Lkpad % 128 || Lkpad < Lk)
     return fail(H3B_ERR_INVALID_ARGUMENT, "Lqpad / Lkpad must be multiples of 128 covering Lq / Lk");
   if (out_row_stride < H * 128 || out_row_stride % 8) return fail(H3B_ERR_INVALID_ARGUMENT, "bad out_row_stride");

@@ -72,6 +72,7 @@ struct PoolArgs {
   uint8_t* similar;      // [H, nb]
   int8_t* q;             // [H, Lpad, 128]
   float* scale;          // [H, nb]
+  int64_t nb_stride;     // blocks between heads in pooled / similar / scale (0: nb)
 };
 cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s);
 struct QkRopeArgs {
@@ -87,6 +88,11 @@ struct QkRopeArgs {
 cudaError_t launch_qk_rmsnorm_rope(const QkRopeArgs& a, cudaStream_t s);
 cudaError_t launch_value_fp8(const void* v, int64_t L, int64_t H, int64_t stride, int64_t Lpad, void* vt,
                              void* vscale, cudaStream_t s);
+// E4M3 codes of `rows` tokens with the caller's per-(head, channel) absmax, written
+// at vt (token column 0 of the slab, row pitch Lpad) in ceil(rows/128) tiles;
+// vscale (optional) receives max(absmax / 2.25, 1e-12)
+cudaError_t launch_value_fp8_given_absmax(const void* v, int64_t rows, int64_t H, int64_t stride, int64_t Lpad,
+                                          const float* absmax, void* vt, float* vscale, cudaStream_t s);
 
 struct MaskArgs {
   const uint16_t* pq;   // [H, Qb, 128]
@@ -101,6 +107,8 @@ struct MaskArgs {
   int temporal_radius, temporal_spatial_radius;
   int64_t frames, frame_tokens, protected_tokens, query_tokens;
   uint32_t* bitmap;
+  const int64_t* q_index;  // [query_tokens] video position of each query, or null (query i at i)
+  int64_t protected_qb;    // query blocks kept dense over every key
 };
 cudaError_t launch_block_mask(const MaskArgs& a, int64_t H, cudaStream_t s);
 cudaError_t launch_bitmap_to_lut(const void* bm, int64_t rows, int64_t Kb, void* lut, void* valid, cudaStream_t s);

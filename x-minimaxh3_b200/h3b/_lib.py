@@ -35,6 +35,8 @@ class MaskParams(ctypes.Structure):
         ("frame_tokens", c_int64),
         ("protected_tokens", c_int64),
         ("query_tokens", c_int64),
+        ("query_indices", c_void_p),
+        ("protected_query_blocks", c_int64),
     ]
 
 
@@ -63,6 +65,10 @@ _SIGNATURES = {
     "h3b_key_mean_no_alloc": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "h3b_pool_sim_quant": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p, c_int64, c_void_p],
+    "h3b_pool_sim_quant_slab": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_int64, c_int64, c_void_p],
+    "h3b_value_fp8_given_absmax": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
+                                   c_void_p],
     "h3b_qk_rmsnorm_rope": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_int, c_float, c_void_p],
     "h3b_value_fp8": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
