@@ -181,6 +181,20 @@ int h3b_pool_sim_quant(const void* x, int64_t L, int64_t H, int64_t x_row_stride
                        int block, const void* thr, void* pooled, void* similar, void* qi8, void* scale,
                        int64_t Lpad, void* stream);
 
+/* Sage per_thread INT8 quantization (qk_quant_gran 3): kind 0 quantizes Q in
+ * 128-row blocks of 32 scale groups (row r of a block in group (r/32)*8 + r%8),
+ * kind 1 quantizes K in 64-row blocks of 4 groups (row r in group (r%8)/2) after
+ * the bf16 mean smoothing bf16(k - mean) (mean: bf16 [H, 128], or NULL for none).
+ * Per group: scale = max|v|/127 + 1e-7 over its rows, code = trunc(v/scale +
+ * 0.5*sign(v)).  x: bf16 NHD [L, H*128] rows of stride x_row_stride; qi8: int8
+ * [H, Lpad, 128] (rows past the last block untouched, the last block's rows >= L
+ * code 0); scale: f32 [H, ceil(L/128)*32] (Q) or [H, ceil(L/64)*4] (K).
+ * Replaces sageattention's per_thread_int8 / quant_query_per_thread_int8_kernel and
+ * quantize_key_sub_mean_per_thread_int8 (model/sage_fused_quant.py:20-162,
+ * 165-283; model/kernels.py:7664-7727). */
+int h3b_quantize_per_thread_int8(const void* x, int64_t L, int64_t H, int64_t x_row_stride, const void* mean,
+                                 int kind, void* qi8, void* scale, int64_t Lpad, void* stream);
+
 /* h3b_pool_sim_quant over one slab of `rows` tokens of a longer sequence, writing
  * into that sequence's arrays: pooled / similar / scale point at the slab's first
  * block of head 0 with `blocks_per_head` blocks between heads, qi8 at the slab's
@@ -267,16 +281,25 @@ int h3b_bitmap_to_lut(const void* bitmap, int64_t rows, int64_t Kb, void* lut, v
  * online softmax, P and V in FP8 E4M3 (tcgen05 kind::f8f6f4), fp32 output
  * accumulation.  Visits only the K blocks whose bit is set in `bitmap`
  * ([H, ceil(Lq/128), ceil(Kb/32)] words) or all of them when bitmap is NULL.
- * q: int8 [H, Lqpad, 128], q_scale f32 [H, ceil(Lq/q_block)] (q_block 32, 64 or 128);
- * k: int8 [H, Lkpad, 128], k_scale f32 [H, ceil(Lk/64)];
+ * q: int8 [H, Lqpad, 128] with q_scale f32 [H, nqs]:
+ *   q_gran 0: one scale per q_block (32, 64 or 128) rows, nqs = ceil(Lq/q_block)
+ *             (Sparge per-block 128; per_warp 32);
+ *   q_gran 1: Sage per_thread, row i in group (i/32)*8 + i%8, nqs = ceil(Lq/128)*32
+ *             (q_block ignored);
+ * k: int8 [H, Lkpad, 128] with k_scale f32:
+ *   k_gran 0: [H, ceil(Lk/64)], one scale per 64-key block;
+ *   k_gran 1: [H, ceil(Lk/64)*4], Sage per_thread, key j in group (j%64 %8)/2 of its
+ *             block (k_scale 16-byte aligned);
  * vt: e4m3 [H, 128, Lkpad], v_scale f32 [H, 128];
  * out: bf16 NHD rows [Lq, H*128] with row stride out_row_stride.
  * Lqpad % 128 == 0, Lkpad % 128 == 0.
- * Replaces sageattn qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf and the
- * Sparge block-sparse variant (model/kernels.py:7645-7661, 3981-3997). */
-int h3b_attention(const void* q, const void* q_scale, int q_block, int64_t Lq, int64_t Lqpad, const void* k,
-                  const void* k_scale, int64_t Lk, int64_t Lkpad, const void* vt, const void* v_scale, int64_t H,
-                  const void* bitmap, float sm_scale, void* out, int64_t out_row_stride, void* stream);
+ * Replaces sageattn qk_int8_sv_f8_accum_f16_fuse_v_scale_attn_inst_buf (its
+ * qk_quant_gran 1 / 2 / 3) and the Sparge block-sparse variant
+ * (model/kernels.py:7645-7661, 7728-7742, 5575-5588, 3981-3997). */
+int h3b_attention(const void* q, const void* q_scale, int q_gran, int q_block, int64_t Lq, int64_t Lqpad,
+                  const void* k, const void* k_scale, int k_gran, int64_t Lk, int64_t Lkpad, const void* vt,
+                  const void* v_scale, int64_t H, const void* bitmap, float sm_scale, void* out,
+                  int64_t out_row_stride, void* stream);
 
 #ifdef __cplusplus
 }

@@ -525,6 +525,65 @@ void h3bo_pool_sim_quant(const uint16_t* x, int64_t L, int64_t H, const uint16_t
     free(v);
 }
 
+/* Sage per_thread INT8 quantization (qk_quant_gran 3), in the scale groups of
+ * q_scale_index / k_scale_index below:
+ *   kind 0 (Q): 128-row blocks of 32 groups, row i in group (i / 32) * 8 + i % 8
+ *              (sageattention's quant_query_per_thread_int8_kernel, BLK = 32 with
+ *              8 row classes: the in-tree callers fix its grid and scale shape,
+ *              model/sage_fused_quant.py:201-222, kernels.py:7700-7725);
+ *   kind 1 (K): 64-row blocks of 4 groups, row j in group (j % 8) / 2, values
+ *              bf16(k - mean) (model/sage_fused_quant.py:20-117).
+ * Per group: scale = max|v| / 127 + 1e-7 over its valid rows (rows >= L count as
+ * 0); code = trunc(v / scale + 0.5 * sign), rows >= L code 0.
+ * qi8: [H, Lpad, 128] with Lpad >= the blocks' rows; scale: [H, blocks * groups]. */
+void h3bo_quant_per_thread(const uint16_t* x, int64_t L, int64_t H, const uint16_t* mean, int kind,
+                           int8_t* qi8, int64_t Lpad, float* scale) {
+    const int D = 128;
+    const int blk = kind == 0 ? 128 : 64, ng = kind == 0 ? 32 : 4;
+    const int64_t nb = (L + blk - 1) / blk;
+    float* v = (float*)malloc(sizeof(float) * (size_t)blk * D);
+    for (int64_t h = 0; h < H; ++h)
+        for (int64_t b = 0; b < nb; ++b) {
+            const int64_t r0 = b * blk;
+            const int valid = (int)((L - r0) < blk ? (L - r0) : blk);
+            float gmax[32];
+            for (int g = 0; g < ng; ++g) gmax[g] = 0.0f;
+            for (int r = 0; r < blk; ++r) {
+                const int g = kind == 0 ? (r / 32) * 8 + (r % 8) : (r % 8) / 2;
+                for (int d = 0; d < D; ++d) {
+                    float val = 0.0f;
+                    if (r < valid) {
+                        val = bf16_to_f32(x[((r0 + r) * H + h) * D + d]);
+                        if (mean) val = bf16r(val - bf16_to_f32(mean[h * D + d]));
+                    }
+                    v[r * D + d] = val;
+                    gmax[g] = fmaxf(gmax[g], fabsf(val));
+                }
+            }
+            float sc[32];
+            for (int g = 0; g < ng; ++g) {
+                sc[g] = gmax[g] / 127.0f + 1e-7f;
+                scale[h * nb * ng + b * ng + g] = sc[g];
+            }
+            for (int r = 0; r < blk; ++r) {
+                const int g = kind == 0 ? (r / 32) * 8 + (r % 8) : (r % 8) / 2;
+                for (int d = 0; d < D; ++d) {
+                    int8_t qv = 0;
+                    if (r < valid) {
+                        float t = v[r * D + d] / sc[g];
+                        t = t + (t >= 0.0f ? 0.5f : -0.5f);
+                        float tr = truncf(t);
+                        if (tr > 127.0f) tr = 127.0f;
+                        if (tr < -127.0f) tr = -127.0f;
+                        qv = (int8_t)tr;
+                    }
+                    qi8[(h * Lpad + r0 + r) * D + d] = qv;
+                }
+            }
+        }
+    free(v);
+}
+
 /* Per-head RMSNorm + split-half partial RoPE, in place (model/layers.py:72-149):
  * n = bf16((x * inv) * w), inv = 1/sqrt(sum(x^2)/128 + eps) with the sum in the
  * warp order of warp_sum128; then for d < r = rot/2:
@@ -764,6 +823,176 @@ void h3bo_attention(const int8_t* q, const float* qscale, int qblk, int64_t Lq, 
                 }
             }
         free(s); free(o);
+    }
+}
+
+/* ------------------------------------------------------------------------- */
+/* Quantized attention with the kernel's own P arithmetic                    */
+/* ------------------------------------------------------------------------- */
+
+/* Scale groups of the Sage quantization granularities (the reference's
+ * qk_quant_gran codes, model/kernels.py:4142-4160, 7652-7660):
+ *   Q  gran 0: rows [g * q_block, (g+1) * q_block) share a scale (per-block 128 /
+ *              64, per_warp 32); index i / q_block, ceil(Lq / q_block) per head;
+ *      gran 1: per_thread -- in each 32-row group the rows with equal i % 8 share a
+ *              scale; index (i / 32) * 8 + i % 8, ceil(Lq / 128) * 32 per head.
+ *   K  gran 0: one scale per 64-key block, index j / 64, ceil(Lk / 64) per head;
+ *      gran 1: per_thread -- in each 64-key block the keys with equal (j % 8) / 2
+ *              share a scale; index (j / 64) * 4 + (j % 8) / 2, ceil(Lk / 64) * 4
+ *              per head (model/sage_fused_quant.py:41-44). */
+static inline int64_t q_scale_index(int64_t i, int q_gran, int q_block) {
+    return q_gran == 1 ? (i / 32) * 8 + (i % 8) : i / q_block;
+}
+static inline int64_t k_scale_index(int64_t j, int k_gran) {
+    return k_gran == 1 ? (j / 64) * 4 + (j % 8) / 2 : j / 64;
+}
+
+/* 2^x on the FMA pipe, the attention kernel's own polynomial (attn.cu exp2_poly,
+ * fitted for that kernel): j = rint(x) through the 1.5 * 2^23 constant, 2^(x - j)
+ * by a degree-3 polynomial, j added to the exponent field; x clamped at -125. */
+static float attn_exp2_poly(float x) {
+    const float kM = 12582912.0f;
+    const float P0 = 0.9999280571937561f, P1 = 0.6932609677314758f, P2 = 0.2426111251115799f,
+                P3 = 0.05517164617776871f;
+    float xp = x > -125.0f ? x : -125.0f;
+    if (x != x) xp = -125.0f;
+    float t = xp + kM;
+    float f = fmaf(t + (-kM), -1.0f, xp);
+    float q = fmaf(fmaf(fmaf(P3, f, P2), f, P1), f, P0);
+    return u2f(f2u(q) + (f2u(t) << 23));
+}
+
+/* 2^x as the kernel's ex2.approx computes it, up to its last-bit error: double
+ * exp2 rounded to float (0 for -inf). */
+static float attn_exp2(float x) {
+    if (x == -INFINITY) return 0.0f;
+    return (float)exp2((double)x);
+}
+
+/* O = softmax(Q K^T * sm_scale) V in the attention kernel's arithmetic (attn.cu):
+ * for each query row, the key blocks its 128-row tile visits (all, or the bitmap's
+ * set bits) in ascending order, two per step (the last step may hold one):
+ *   v_j   = float(1.5 * 2^23 + S_j), S_j the exact int32 Q.K dot product
+ *   c     = max(qs * (sm_scale * log2 e) * ks, 1e-30)      (per scale group)
+ *   tmax  = max over the step's groups of (max_j v_j - 1.5 * 2^23) * c
+ *   m     = tmax if tmax > m + 2 else m (lazy running max); alpha = 2^(m_old - m)
+ *   x_j   = fma(v_j, c, (log2 112 - m) - 1.5 * 2^23 * c)
+ *   P_j   = 2^x_j: the polynomial above on columns 6, 7 of every 16 of a block,
+ *           ex2 (hardware, modelled by a correctly rounded exp2) on the others
+ *   l     = l * alpha + (sum of the step's fp32 P_j in the kernel's order)
+ *   O     = O * alpha + sum_j E4M3(P_j) * E4M3(V_j) * (accumulated in double here;
+ *           fp32 in tensor memory on the GPU)
+ *   out   = bf16(float(O) * (1 / l) * v_scale[d])
+ * Keys >= Lk are -inf (P = 0 on ex2 columns, 2^-125 on polynomial columns, as on
+ * the GPU).  Rows whose tile visits no block are 0.  The GPU result differs from
+ * this only by ex2.approx's last bits and the tensor core's fp32 accumulation. */
+void h3bo_attention_kernel(const int8_t* q, const float* qscale, int q_gran, int q_block, int64_t Lq,
+                           int64_t Lqpad, const int8_t* k, const float* kscale, int k_gran, int64_t Lk,
+                           int64_t Lkpad, const uint8_t* vt, const float* vscale, int64_t H,
+                           const uint32_t* bitmap, float sm_scale, uint16_t* out) {
+    const int D = 128;
+    const float kM = 12582912.0f, kLog2_112 = 6.807354922057604f, kTau = 2.0f;
+    const int64_t Kb = (Lk + 63) / 64, Qb = (Lq + 127) / 128, words = (Kb + 31) / 32;
+    const int64_t nqs = q_gran == 1 ? Qb * 32 : (Lq + q_block - 1) / q_block;
+    const int64_t nks = k_gran == 1 ? Kb * 4 : Kb;
+    const float scale_log2 = sm_scale * 1.4426950408889634f;
+    float vlut[256];
+    for (int i = 0; i < 256; ++i) vlut[i] = h3bo_e4m3_to_f32((uint8_t)i);
+#pragma omp parallel
+    {
+        int64_t* blocks = (int64_t*)malloc(sizeof(int64_t) * (size_t)(Kb + 1));
+        double* o = (double*)malloc(sizeof(double) * D);
+        float vrow[128];
+        uint8_t pq8[128];
+#pragma omp for schedule(dynamic) collapse(2)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t i = 0; i < Lq; ++i) {
+                const int8_t* qr = q + (h * Lqpad + i) * D;
+                const float qs = qscale[h * nqs + q_scale_index(i, q_gran, q_block)];
+                const float qsl = qs * scale_log2;
+                int64_t nb = 0;
+                const uint32_t* brow = bitmap ? bitmap + (h * Qb + i / 128) * words : NULL;
+                for (int64_t b = 0; b < Kb; ++b)
+                    if (!brow || ((brow[b / 32] >> (b % 32)) & 1u)) blocks[nb++] = b;
+                float m = -INFINITY, l = 0.0f;
+                for (int d = 0; d < D; ++d) o[d] = 0.0;
+                for (int64_t st = 0; st < nb; st += 2) {
+                    const int nblk = st + 1 < nb ? 2 : 1;
+                    float v[2][64], c[2][4];
+                    float tmax = -INFINITY;
+                    for (int u = 0; u < nblk; ++u) {
+                        const int64_t b = blocks[st + u];
+                        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                        for (int g = 0; g < 4; ++g) {
+                            const float ks = kscale[h * nks + (k_gran == 1 ? b * 4 + g : b)];
+                            float cc = qsl * ks;
+                            c[u][g] = cc > 1e-30f ? cc : 1e-30f;
+                        }
+                        for (int cidx = 0; cidx < 64; ++cidx) {
+                            const int64_t j = b * 64 + cidx;
+                            if (j >= Lk) { v[u][cidx] = -INFINITY; continue; }
+                            const int8_t* kr = k + (h * Lkpad + j) * D;
+                            int32_t acc = 0;
+                            for (int d = 0; d < D; ++d) acc += (int32_t)qr[d] * (int32_t)kr[d];
+                            v[u][cidx] = kM + (float)acc;   /* exact: |acc| < 2^22 */
+                            const int g = k_gran == 1 ? (cidx % 8) / 2 : 0;
+                            if (v[u][cidx] > mx[g]) mx[g] = v[u][cidx];
+                        }
+                        for (int g = 0; g < (k_gran == 1 ? 4 : 1); ++g)
+                            if (mx[g] != -INFINITY) {
+                                const float t = (mx[g] - kM) * c[u][g];
+                                if (t > tmax) tmax = t;
+                            }
+                    }
+                    const float m_new = tmax > m + kTau ? tmax : m;
+                    float alpha = 1.0f;
+                    if (m_new != m) {
+                        alpha = attn_exp2(m - m_new);
+                        m = m_new;
+                        for (int d = 0; d < D; ++d) o[d] = (double)((float)o[d] * alpha);
+                    }
+                    const float off = kLog2_112 - m;
+                    float psum = 0.0f;
+                    for (int u = 0; u < nblk; ++u) {
+                        const int64_t b = blocks[st + u];
+                        float oo[4];
+                        for (int g = 0; g < 4; ++g) oo[g] = off - kM * c[u][g];
+                        float p[64];
+                        for (int cidx = 0; cidx < 64; ++cidx) {
+                            const int g = k_gran == 1 ? (cidx % 8) / 2 : 0;
+                            const float x = fmaf(v[u][cidx], c[u][g], oo[g]);
+                            const int poly = (cidx % 16) == 6 || (cidx % 16) == 7;
+                            p[cidx] = poly ? attn_exp2_poly(x) : attn_exp2(x);
+                        }
+                        /* the kernel's order: four fp32 accumulators over packed pairs */
+                        float a0x = 0.f, a0y = 0.f, a1x = 0.f, a1y = 0.f;
+                        for (int cb = 0; cb < 64; cb += 8) {
+                            a0x = a0x + p[cb + 0]; a0y = a0y + p[cb + 1];
+                            a1x = a1x + p[cb + 2]; a1y = a1y + p[cb + 3];
+                            a0x = a0x + p[cb + 4]; a0y = a0y + p[cb + 5];
+                            a1x = a1x + p[cb + 6]; a1y = a1y + p[cb + 7];
+                        }
+                        const float bsum = (a0x + a1x) + (a0y + a1y);
+                        psum = u == 0 ? bsum : psum + bsum;
+                        for (int cidx = 0; cidx < 64; ++cidx) {
+                            pq8[cidx] = h3bo_f32_to_e4m3(p[cidx]);
+                        }
+                        for (int cidx = 0; cidx < 64; ++cidx) {
+                            const int64_t j = b * 64 + cidx;
+                            const float pe = vlut[pq8[cidx]];
+                            if (pe == 0.0f) continue;
+                            for (int d = 0; d < D; ++d) vrow[d] = vlut[vt[(h * D + d) * Lkpad + j]];
+                            for (int d = 0; d < D; ++d) o[d] += (double)pe * (double)vrow[d];
+                        }
+                    }
+                    l = l * alpha + psum;
+                }
+                uint16_t* dst = out + (i * H + h) * D;
+                if (nb == 0) { for (int d = 0; d < D; ++d) dst[d] = 0; continue; }
+                const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+                for (int d = 0; d < D; ++d) dst[d] = f32_to_bf16(((float)o[d] * inv_l) * vscale[h * D + d]);
+            }
+        free(blocks); free(o);
     }
 }
 

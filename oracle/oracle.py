@@ -285,3 +285,54 @@ def attention(q_i8, q_scale, qblk, Lq, k_i8, k_scale, Lk, vt, v_scale, bitmap=No
                          _p(_c(v_scale, np.float32)), I64(H), _p(_c(bitmap, np.uint32)),
                          ctypes.c_float(sm_scale), _p(out))
     return out
+
+
+def attention_kernel(q_i8, q_scale, Lq, k_i8, k_scale, Lk, vt, v_scale, bitmap=None, sm_scale=None, *,
+                     q_gran=0, q_block=128, k_gran=0):
+    """Attention in the GPU kernel's own arithmetic (h3bo_attention_kernel): lazy
+    running max, P = 2^x * 112 rounded to E4M3, fp32 row sums in the kernel's order.
+    q_gran 0: q_block-row scale groups, 1: Sage per_thread; k_gran 0: per 64-key
+    block, 1: Sage per_thread (4 groups per block)."""
+    q = _c(q_i8, np.int8)
+    k = _c(k_i8, np.int8)
+    H, Lqpad, D = q.shape
+    Lkpad = k.shape[1]
+    if sm_scale is None:
+        sm_scale = 1.0 / np.sqrt(D)
+    if H > 1:
+        # one call per head on a thread each (ctypes drops the GIL during the call)
+        from concurrent.futures import ThreadPoolExecutor
+
+        qs, ks, vsc = _c(q_scale, np.float32), _c(k_scale, np.float32), _c(v_scale, np.float32)
+        bm = _c(bitmap, np.uint32)
+        vt = _c(vt, np.uint8)
+
+        def one(h):
+            return attention_kernel(q[h:h + 1], qs[h:h + 1], Lq, k[h:h + 1], ks[h:h + 1], Lk, vt[h:h + 1],
+                                    vsc[h:h + 1], None if bm is None else bm[h:h + 1], sm_scale, q_gran=q_gran,
+                                    q_block=q_block, k_gran=k_gran)
+
+        with ThreadPoolExecutor(max_workers=min(H, os.cpu_count() or 1)) as ex:
+            return np.concatenate(list(ex.map(one, range(H))), axis=1)
+    out = np.empty((Lq, H, D), np.uint16)
+    lib().h3bo_attention_kernel(_p(q), _p(_c(q_scale, np.float32)), ctypes.c_int(q_gran), ctypes.c_int(q_block),
+                                I64(Lq), I64(Lqpad), _p(k), _p(_c(k_scale, np.float32)), ctypes.c_int(k_gran),
+                                I64(Lk), I64(Lkpad), _p(_c(vt, np.uint8)), _p(_c(v_scale, np.float32)), I64(H),
+                                _p(_c(bitmap, np.uint32)), ctypes.c_float(sm_scale), _p(out))
+    return out
+
+
+def quant_per_thread(x_bf16, kind: int, mean=None):
+    """Sage per_thread INT8 (h3bo_quant_per_thread): kind 0 Q (128-row blocks, 32
+    groups), kind 1 K (64-row blocks, 4 groups, values bf16(k - mean))."""
+    x = _c(x_bf16, np.uint16)
+    L, H, D = x.shape
+    blk, ng = (128, 32) if kind == 0 else (64, 4)
+    nb = (L + blk - 1) // blk
+    Lpad = (L + 127) // 128 * 128
+    q = np.empty((H, Lpad, D), np.int8)
+    q[:, nb * blk:] = 0
+    sc = np.empty((H, nb * ng), np.float32)
+    lib().h3bo_quant_per_thread(_p(x), I64(L), I64(H), _p(_c(mean, np.uint16)), ctypes.c_int(kind), _p(q),
+                                I64(Lpad), _p(sc))
+    return q, sc

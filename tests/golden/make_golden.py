@@ -28,6 +28,8 @@ reference function that produced it:
   qk_rope.npz         apply_qknorm_rope on CPU bf16 tensors with the engine's packed split-half
                       rotation table (model/layers.py:60-118: rope_rotation_table, F.rms_norm,
                       rotate_table), rotary widths 128 and 96
+  sage_k_per_thread.npz  sage_fused_quant.quantize_key_sub_mean_per_thread_int8 under
+                      TRITON_INTERPRET=1 (model/sage_fused_quant.py:20-162), Lk 197 / 64 / 1000
   mask_topk.npz       SplitModalityProtectedSpargeAttentionBackend.long_sequence_video_queries
                       (model/kernels.py:3668-3997) with the two absent Sparge helpers replaced
                       by recorders (fill: set the first `count` sorted indices; LUT: capture
@@ -203,6 +205,32 @@ def gen_sparge():
          pk=bits(pk[0]), sk=sk[0].numpy().astype(np.uint8), kq=kq[0].numpy(), ks=ks[0].numpy(),
          kb=bits(kb[0]), thr2=thr2.numpy(), pb=bits(pb[0]), sb=sb[0].numpy().astype(np.uint8),
          qb=qb[0].numpy(), sbs=sbs[0].numpy())
+
+
+def gen_sage_k():
+    """Sage per_thread K quantization with mean smoothing: the in-tree Triton kernel
+    (model/sage_fused_quant.py:20-162) under the interpreter, on the reference test's
+    ragged non-zero-mean inputs (tests/native_engine/test_sage_fused_quant.py:14-38)."""
+    from h3serve.native_engine.model.sage_fused_quant import quantize_key_sub_mean_per_thread_int8
+
+    g = torch.Generator().manual_seed(82736)
+    H, D = 4, 128
+    out = {}
+    for Lk in (197, 64, 1000):
+        k = (torch.randn(1, Lk, H, D, generator=g) * 0.125 + 5.0).to(torch.bfloat16)
+        kmean = k.mean(dim=1, keepdim=True)
+        q8 = torch.empty_like(k, dtype=torch.int8)
+        sc = torch.empty((1, H, (Lk + 63) // 64 * 4), dtype=torch.float32)
+        # The interpreter keeps bf16 as raw uint16 and subtracts the bit patterns;
+        # fp32 copies of the same bf16 values reproduce the kernel's arithmetic
+        # exactly: the fp32 difference of two bf16 numbers of this range is exact,
+        # and the kernel's own .to(bf16) then rounds it as on the GPU.
+        quantize_key_sub_mean_per_thread_int8(k.float(), kmean.float(), q8, sc)
+        out[f"k{Lk}"] = bits(k[0])
+        out[f"kmean{Lk}"] = bits(kmean[0, 0])
+        out[f"kq{Lk}"] = q8[0].numpy()
+        out[f"ks{Lk}"] = sc[0].numpy()
+    save("sage_k_per_thread.npz", **out)
 
 
 def gen_rms_adaln():
@@ -399,6 +427,6 @@ if __name__ == "__main__":
     torch.manual_seed(0)
     only = sys.argv[2:]
     for fn in (gen_quant, gen_convrot, gen_act, gen_w4, gen_linear, gen_sparge, gen_lut, gen_mask, gen_block_ckpt,
-               gen_qk_rope, gen_rms_adaln):
+               gen_qk_rope, gen_rms_adaln, gen_sage_k):
         if not only or fn.__name__ in only:
             fn()

@@ -52,8 +52,13 @@ def test_unsupported_shapes_are_rejected():
     assert lib().h3b_int8_gemm_dequant(dummy, dummy, dummy, dummy, 1, None, dummy, 8, 8, 24, 8, 2, None) == -2
     assert lib().h3b_int8_gemm_dequant(dummy, dummy, dummy, dummy, 1, None, dummy, 8, 8, 32, 8, 0, None) == -2
     assert lib().h3b_dequant_int4_grouped_to_int8(dummy, dummy, 0, None, dummy, 8, 64, 3, None) == -2
-    assert lib().h3b_attention(dummy, dummy, 96, 10, 128, dummy, dummy, 10, 128, dummy, dummy, 1, None,
+    assert lib().h3b_attention(dummy, dummy, 0, 96, 10, 128, dummy, dummy, 0, 10, 128, dummy, dummy, 1, None,
                                0.1, dummy, 128, None) == -2
+    assert lib().h3b_attention(dummy, dummy, 2, 128, 10, 128, dummy, dummy, 0, 10, 128, dummy, dummy, 1, None,
+                               0.1, dummy, 128, None) == -1
+    assert lib().h3b_attention(dummy, ctypes.c_void_p(20), 0, 128, 10, 128, dummy, ctypes.c_void_p(20), 1, 10, 128,
+                               dummy, dummy, 1, None, 0.1, dummy, 128, None) == -2
+    assert lib().h3b_quantize_per_thread_int8(dummy, 10, 1, 128, None, 2, dummy, dummy, 128, None) == -1
 
 
 def test_qkv_qk_rope_entry_rejects_what_it_does_not_take():

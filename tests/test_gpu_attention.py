@@ -1,14 +1,15 @@
 """GPU parity of the attention preparation, the Sparge mask and the tcgen05
 quantized attention kernel.
 
-Preparation (K mean, pool / similarity / INT8, V FP8), the block mask and the
-LUT are bit-exact against the CPU oracle.  The attention output is compared
-with the oracle's exact-softmax attention over the same quantized Q / K / V:
-cos >= 0.999 and rel-L2 <= 3e-2.  The rel-L2 floor is the E4M3 rounding of P
-(3 mantissa bits: up to 6.25 % per probability, about 3.6 % RMS), the P format
-of the reference's sm89 kernel too; it does not shrink with sequence length
-because the output's own magnitude shrinks at the same rate, so the kernel
-sits at about 2.5 % against exact softmax at every L tested.
+Preparation (K mean, pool / similarity / INT8, Sage per_thread INT8, V FP8), the
+block mask and the LUT are bit-exact against the CPU oracle.  The attention output
+is compared with the oracle in the kernel's own arithmetic -- P = 2^x * 112 rounded
+to E4M3 under the lazy running max, fp32 row sums in the kernel's order -- at
+rel-L2 <= 5e-3 and cos >= 0.9999 (what is left is ex2.approx's last bits and the
+tensor core's fp32 accumulation order), and with exact softmax over the same
+quantized Q / K / V at cos >= 0.999.  (The E4M3 rounding of P, 3 mantissa bits, is
+the P format of the reference's sm89 kernel too and alone puts about 2.5 % rel-L2
+between any such kernel and exact softmax.)
 """
 
 import math
@@ -18,7 +19,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import bits, cosine, from_bits, rel_l2
+from gpu_util import assert_attention_parity, bits, cosine, from_bits, rel_l2
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -178,10 +179,77 @@ def test_bitmap_to_lut_bit_exact(attn):
     np.testing.assert_array_equal(lut.cpu().numpy(), lo)
 
 
-def _oracle_attention(pq, pk, pv, bitmap=None):
-    return O.attention(pq.qi8.cpu().numpy(), pq.scale.cpu().numpy(), pq.block, pq.tokens, pk.qi8.cpu().numpy(),
-                       pk.scale.cpu().numpy(), pk.tokens, pv.vt.cpu().numpy(), pv.scale.cpu().numpy(),
-                       None if bitmap is None else bitmap.cpu().numpy().view(np.uint32))
+@pytest.mark.parametrize("L,H,Lk", [(1000, 2, None), (128, 1, None), (300, 2, 77), (2048, 1, None), (64, 1, 1)])
+def test_dense_attention_parity(attn, L, H, Lk):
+    _, pq, pk, pv, _ = _prepared_pair(attn, L, H, seed=L + H, Lk=Lk)
+    out = attn.attention(pq, pk, pv)
+    assert_attention_parity(out, pq, pk, pv)
+
+
+@pytest.mark.parametrize("sparse", [False, True])
+def test_long_sequence_attention_parity(attn, sparse):
+    """L = 8192: sampled tiles (first pair, a middle pair, the last) on both heads."""
+    _, pq, pk, pv, _ = _prepared_pair(attn, 8192, 2, seed=77)
+    bm = attn.block_mask(pq, pk, attn.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True)) \
+        if sparse else None
+    out = attn.attention(pq, pk, pv, bm)
+    assert_attention_parity(out, pq, pk, pv, bm, tiles=(0, 1, 30, 31, 63))
+
+
+@pytest.mark.parametrize("block", [64, 32])
+def test_dense_attention_q_groups(attn, block):
+    """Per-64-token Q blocks and Sage per_warp 32-row groups."""
+    q, k, v = qkv(700, 2, seed=5 + block)
+    pv = attn.prepare_values(v.cuda())
+    pk, _ = attn.prepare_keys(k.cuda())
+    pq = attn.prepare_queries(q.cuda(), block=block)
+    out = attn.attention(pq, pk, pv)
+    assert_attention_parity(out, pq, pk, pv)
+
+
+@pytest.mark.parametrize("cfg", [dict(mode="topk", budget=0.3), dict(mode="cdf", budget=0.6, keep_first_column=True,
+                                                                     keep_diagonal=True)])
+def test_sparse_attention_parity(attn, cfg):
+    _, pq, pk, pv, _ = _prepared_pair(attn, 1500, 2, seed=99)
+    bm = attn.block_mask(pq, pk, attn.MaskConfig(**cfg))
+    out = attn.attention(pq, pk, pv, bm)
+    assert_attention_parity(out, pq, pk, pv, bm)
+
+
+@pytest.mark.parametrize("L", [197, 64, 1000])
+def test_sage_k_per_thread_golden(attn, L):
+    """Sage per_thread K quantization on the GPU equals the reference's in-tree kernel
+    (model/sage_fused_quant.py:20-162; fixture made by tests/golden/make_golden.py)."""
+    z = np.load(os.path.join(G, "sage_k_per_thread.npz"))
+    pk = attn.quantize_per_thread(from_bits(z[f"k{L}"]), "k", from_bits(z[f"kmean{L}"]))
+    np.testing.assert_array_equal(pk.qi8[:, :L].cpu().numpy().transpose(1, 0, 2), z[f"kq{L}"])
+    np.testing.assert_array_equal(pk.scale.cpu().numpy(), z[f"ks{L}"])
+
+
+@pytest.mark.parametrize("L,H", [(1000, 3), (131, 2), (4100, 1)])
+def test_quant_per_thread_bit_exact(attn, L, H):
+    q, k, _ = qkv(L, H, seed=L)
+    mean = attn.key_mean(k.cuda())
+    pq = attn.quantize_per_thread(q.cuda(), "q")
+    pk = attn.quantize_per_thread(k.cuda(), "k", mean)
+    for pb, x, kind, m in ((pq, q, 0, None), (pk, k, 1, bits(mean))):
+        rq, rs = O.quant_per_thread(bits(x), kind, m)
+        np.testing.assert_array_equal(pb.qi8.cpu().numpy(), rq)
+        np.testing.assert_array_equal(pb.scale.cpu().numpy(), rs)
+
+
+@pytest.mark.parametrize("L,H,Lk", [(1000, 2, None), (300, 2, 77), (4096, 1, None)])
+def test_dense_attention_per_thread(attn, L, H, Lk):
+    """Sage per_thread granularity (the reference's dense default, qk_quant_gran 3):
+    4-row Q scale groups, 16-key K groups per 64-key block."""
+    q, k, v = qkv(L, H, seed=3 * L, Lk=Lk)
+    backend = attn.SageAttentionB200(qk_quant_gran="per_thread")
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    out = backend(qc, kc, vc)
+    pq, pk, pv = backend.quantize_queries(qc), backend.quantize_keys(kc), attn.prepare_values(vc)
+    assert pq.gran == 1 and pk.gran == 1
+    assert torch.equal(out, attn.attention(pq, pk, pv))
+    assert_attention_parity(out, pq, pk, pv)
 
 
 def _sdpa(q, k, v):
@@ -190,77 +258,16 @@ def _sdpa(q, k, v):
     return (s.softmax(-1) @ vf).permute(1, 0, 2)
 
 
-@pytest.mark.parametrize("L,H,Lk", [(1000, 2, None), (128, 1, None), (300, 2, 77), (2048, 1, None), (64, 1, 1)])
-def test_dense_attention_vs_oracle_and_fp32(attn, L, H, Lk):
-    (q, k, v), pq, pk, pv, _ = _prepared_pair(attn, L, H, seed=L + H, Lk=Lk)
-    out = attn.attention(pq, pk, pv)
-    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv))
-    o = out.float().cpu()
-    assert cosine(o, ref) >= 0.999
-    assert rel_l2(o, ref) <= 3e-2
-    exact = _sdpa(q, k, v)
-    assert cosine(o, exact) >= 0.99
-
-
-def _dequantized_attention_fp32(pq, pk, pv, bitmap=None):
-    """fp32 torch attention over the dequantized operands (the oracle's math on the GPU)."""
-    H = pq.qi8.shape[0]
-    Lq, Lk = pq.tokens, pk.tokens
-    qs = pq.scale.repeat_interleave(pq.block, dim=1)[:, :Lq]
-    ks = pk.scale.repeat_interleave(64, dim=1)[:, :Lk]
-    q = pq.qi8[:, :Lq].float() * qs[..., None]
-    k = pk.qi8[:, :Lk].float() * ks[..., None]
-    lut = torch.tensor([O.lib().h3bo_e4m3_to_f32(i) for i in range(256)], device=q.device)
-    v = lut[pv.vt[:, :, :Lk].long()].transpose(1, 2) * pv.scale[:, None, :]
-    s = q @ k.transpose(1, 2) / math.sqrt(128)
-    if bitmap is not None:
-        words = bitmap.view(torch.int32)
-        Kb = (Lk + 63) // 64
-        bits = ((words[..., :, None] >> torch.arange(32, device=q.device)) & 1).reshape(H, words.shape[1], -1)[..., :Kb]
-        keep = bits.bool().repeat_interleave(128, 1)[:, :Lq].repeat_interleave(64, 2)[..., :Lk]
-        s = s.masked_fill(~keep, float("-inf"))
-    return (s.softmax(-1) @ v).permute(1, 0, 2)
-
-
-@pytest.mark.parametrize("sparse", [False, True])
-def test_long_sequence_attention_vs_fp32(attn, sparse):
-    """L = 8192 (too long for the C oracle): cos >= 0.999 and rel-L2 <= 3e-2
-    against fp32 torch attention over the same dequantized operands."""
-    (q, k, v), pq, pk, pv, _ = _prepared_pair(attn, 8192, 2, seed=77)
-    bm = attn.block_mask(pq, pk, attn.MaskConfig("cdf", 0.6, keep_first_column=True, keep_diagonal=True)) \
-        if sparse else None
-    out = attn.attention(pq, pk, pv, bm).float()
-    ref = _dequantized_attention_fp32(pq, pk, pv, bm)
-    assert cosine(out, ref) >= 0.999
-    assert rel_l2(out, ref) <= 3e-2
-
-
-def test_dense_attention_q_block_64(attn):
-    q, k, v = qkv(700, 2, seed=5)
-    pv = attn.prepare_values(v.cuda())
-    pk, _ = attn.prepare_keys(k.cuda())
-    pq = attn.prepare_queries(q.cuda(), block=64)
-    out = attn.attention(pq, pk, pv).float().cpu()
-    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv))
-    assert cosine(out, ref) >= 0.999 and rel_l2(out, ref) <= 3e-2
-
-
-@pytest.mark.parametrize("cfg", [dict(mode="topk", budget=0.3), dict(mode="cdf", budget=0.6, keep_first_column=True,
-                                                                     keep_diagonal=True)])
-def test_sparse_attention_vs_oracle(attn, cfg):
-    (q, k, v), pq, pk, pv, _ = _prepared_pair(attn, 1500, 2, seed=99)
-    bm = attn.block_mask(pq, pk, attn.MaskConfig(**cfg))
-    out = attn.attention(pq, pk, pv, bm).float().cpu()
-    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv, bm))
-    assert cosine(out, ref) >= 0.999
-    assert rel_l2(out, ref) <= 3e-2
-
-
 def test_backends_are_attention_callables(attn):
+    """The backends against fp32 attention on the unquantized inputs: INT8 Q / K, FP8 P
+    and V together stay within cos 0.99 (the per-stage bounds are in the tests above)."""
     q, k, v = qkv(513, 2, seed=3)
     dense = attn.SageAttentionB200()(q.cuda(), k.cuda(), v.cuda())
     assert dense.shape == (513, 2, 128) and dense.dtype == torch.bfloat16
     assert cosine(dense.float().cpu(), _sdpa(q, k, v)) >= 0.99
+    for gran in ("per_thread", "per_warp"):
+        o = attn.SageAttentionB200(qk_quant_gran=gran)(q.cuda(), k.cuda(), v.cuda())
+        assert cosine(o.float().cpu(), _sdpa(q, k, v)) >= 0.99
     sparse = attn.SpargeAttentionB200(attn.MaskConfig("topk", 1.0))(q.cuda(), k.cuda(), v.cuda())
     assert cosine(sparse.float().cpu(), dense.float().cpu()) >= 0.9999
 
@@ -358,6 +365,5 @@ def test_dense_attention_per_warp_q(attn):
     pk, _ = attn.prepare_keys(k.cuda())
     pq = attn.prepare_queries(q.cuda(), block=32)
     assert pq.scale.shape == (2, 22)
-    out = attn.attention(pq, pk, pv).float().cpu()
-    ref = O.bf16_bits_to_f32(_oracle_attention(pq, pk, pv))
-    assert cosine(out, ref) >= 0.999 and rel_l2(out, ref) <= 3e-2
+    out = attn.attention(pq, pk, pv)
+    assert_attention_parity(out, pq, pk, pv)

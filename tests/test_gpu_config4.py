@@ -7,9 +7,10 @@ random separable cosine modes, projected to the head dimension by a [16, 128]
 N(0, 1/16) matrix per head; V is N(0, 1).  Two heads keep the CPU oracle's
 share of the test to seconds.  Checked:
   * the block bitmap equals the CPU oracle's selector bit for bit;
-  * the attention output of three sampled query tiles (first, middle, last)
-    is within cos >= 0.999 / rel-L2 <= 3e-2 of fp32 attention over the same
-    dequantized operands restricted to the selected blocks (the tolerance of
+  * the attention output of sampled query tiles (first pair, middle, last) is
+    within rel-L2 <= 5e-3 / cos >= 0.9999 of the CPU oracle in the kernel's own
+    arithmetic, and within cos >= 0.999 of exact fp32 softmax over the same
+    dequantized operands restricted to the selected blocks (the tolerances of
     the other attention tests);
   * no bounded wait timed out.
 """
@@ -20,7 +21,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import bits, cosine, rel_l2
+from gpu_util import assert_attention_parity, bits
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -42,25 +43,6 @@ def smooth_field(grid, heads, gen):
     proj = torch.randn(heads, 16, 128, generator=gen) / 4.0
     x = torch.einsum("lm,hmd->lhd", field, proj)
     return (x + 0.3 * torch.randn(x.shape, generator=gen)).to(torch.bfloat16)
-
-
-def sampled_reference(pq, pk, pv, bitmap, tiles):
-    """fp32 attention over the dequantized operands for the query rows of `tiles`."""
-    Lq, Lk = pq.tokens, pk.tokens
-    rows = torch.cat([torch.arange(t * 128, min(Lq, t * 128 + 128)) for t in tiles]).cuda()
-    qs = pq.scale.repeat_interleave(pq.block, dim=1)[:, rows]
-    ks = pk.scale.repeat_interleave(64, dim=1)[:, :Lk]
-    q = pq.qi8[:, rows].float() * qs[..., None]
-    k = pk.qi8[:, :Lk].float() * ks[..., None]
-    lut = torch.tensor([O.lib().h3bo_e4m3_to_f32(i) for i in range(256)], device=q.device)
-    v = lut[pv.vt[:, :, :Lk].long()].transpose(1, 2) * pv.scale[:, None, :]
-    s = q @ k.transpose(1, 2) / math.sqrt(128)
-    words = bitmap.view(torch.int32)[:, rows // 128]     # [H, rows, words]
-    Kb = (Lk + 63) // 64
-    keep = ((words[..., :, None] >> torch.arange(32, device=q.device)) & 1).reshape(H, len(rows), -1)[..., :Kb]
-    keep = keep.bool().repeat_interleave(64, 2)[..., :Lk]
-    s = s.masked_fill(~keep, float("-inf"))
-    return (s.softmax(-1) @ v).permute(1, 0, 2), rows
 
 
 def test_config4_sparge_full_length():
@@ -90,8 +72,5 @@ def test_config4_sparge_full_length():
     np.testing.assert_array_equal(bm.cpu().numpy().view(np.uint32), ref)
 
     out = A.attention(pq, pk, pv, bm)
-    want, rows = sampled_reference(pq, pk, pv, bm, tiles=(0, 857, 1715))
-    got = out[rows].float()
-    assert cosine(got, want) >= 0.999
-    assert rel_l2(got, want) <= 3e-2
+    assert_attention_parity(out, pq, pk, pv, bm, tiles=(0, 1, 857, 1715))
     assert h3b.device_status(0) == 0

@@ -277,3 +277,43 @@ def test_value_fp8_vs_reference_formula_in_torch():
                 assert not vt[h, d].any() and vs[h, d] == 0
     np.testing.assert_array_equal(vs[live], (absmax / 2.25).numpy()[live])
     assert not vt[:, :, L:].any()
+
+
+def test_sage_k_per_thread_golden():
+    """Sage per_thread K quantization with mean smoothing: the oracle equals the
+    reference's in-tree kernel (model/sage_fused_quant.py:20-162) code for code and
+    scale for scale, on the reference test's ragged non-zero-mean inputs."""
+    z = np.load(os.path.join(G, "sage_k_per_thread.npz"))
+    for L in (197, 64, 1000):
+        q, sc = O.quant_per_thread(z[f"k{L}"], 1, z[f"kmean{L}"])
+        np.testing.assert_array_equal(q[:, :L].transpose(1, 0, 2), z[f"kq{L}"])
+        np.testing.assert_array_equal(sc, z[f"ks{L}"])
+        assert not q[:, L:].any()
+
+
+def test_kernel_order_attention_models_the_p_format():
+    """The kernel-order oracle (P -> E4M3 under the lazy running max) sits at the
+    E4M3 format error from exact softmax over the same operands (rel-L2 about 2.5 %,
+    cos >= 0.999), for per-block and per_thread scale groups alike."""
+    g = np.random.default_rng(0)
+    L, H = 300, 2
+    q = O.f32_to_bf16_bits(g.standard_normal((L, H, 128)).astype(np.float32))
+    k = O.f32_to_bf16_bits((g.standard_normal((L, H, 128)) + 3 * g.standard_normal((1, H, 128))).astype(np.float32))
+    v = O.f32_to_bf16_bits(g.standard_normal((L, H, 128)).astype(np.float32))
+    mean = O.key_mean(k)
+    vt, vs = O.value_fp8(v)
+    thr = np.full(H, -0.1, np.float32)
+    _, _, qb, qbs = O.pool_sim_quant(q, 128, thr)
+    _, _, kb, kbs = O.pool_sim_quant(k, 64, thr, mean)
+    pad = lambda a: np.concatenate([a, np.zeros((H, (-a.shape[1]) % 128, 128), np.int8)], 1)
+    qb, kb = pad(qb), pad(kb)
+    exact = O.bf16_bits_to_f32(O.attention(qb, qbs, 128, L, kb, kbs, L, vt, vs))
+    fmt = O.bf16_bits_to_f32(O.attention_kernel(qb, qbs, L, kb, kbs, L, vt, vs))
+    rel = np.linalg.norm(fmt - exact) / np.linalg.norm(exact)
+    cos = float((fmt * exact).sum() / np.linalg.norm(fmt) / np.linalg.norm(exact))
+    assert 0.01 < rel < 0.04 and cos >= 0.999
+    qt, qts = O.quant_per_thread(q, 0)
+    kt, kts = O.quant_per_thread(k, 1, mean)
+    fmt_t = O.bf16_bits_to_f32(O.attention_kernel(qt, qts, L, kt, kts, L, vt, vs, q_gran=1, k_gran=1))
+    cos_t = float((fmt_t * exact).sum() / np.linalg.norm(fmt_t) / np.linalg.norm(exact))
+    assert cos_t >= 0.999

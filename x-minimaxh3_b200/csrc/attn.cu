@@ -6,6 +6,9 @@
 //       float 1.5*2^23 + S (|S| < 2^22), so S needs no integer->float conversion
 //       and the block maximum is an integer maximum of the raw bits
 //   P = exp2(S * qs * ks * scale * log2 e - m) * 112 -> E4M3 (shared memory);
+//       qs per query row group (q_block rows, or Sage per_thread: rows of equal
+//       r % 8 in each 32), ks per 64-key block or per_thread group (keys of equal
+//       (j % 8) / 2 in each 64-key block: KG = 4);
 //       m is a lazily updated running max: it moves (to the tile max) only when
 //       a tile's scores exceed it by more than kTau = 2, so P <= 2^kTau * 112 =
 //       448, the E4M3 maximum, and the O rescale in tensor memory is rare.
@@ -148,6 +151,16 @@ __device__ __forceinline__ float ld_early(const float* p) {
   asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
   return v;
 }
+// KG consecutive scales (KG = 1 or 4; 16-byte aligned for 4), loaded early
+template <int KG>
+__device__ __forceinline__ void ld_early_kg(const float* p, float (&v)[KG]) {
+  if constexpr (KG == 1) {
+    v[0] = ld_early(p);
+  } else {
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "l"(p));
+  }
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -217,13 +230,47 @@ __device__ __forceinline__ int raw_max_ragged(uint32_t (&s)[128], int n) {
   }
   return m0;
 }
+// Sage per_thread K scales: four scale groups per 64-key block, column c in group
+// (c % 8) / 2 -- the column pairs (2g, 2g + 1) of every 8-column chunk, which are
+// exactly the packed pairs the exponential below works on.  Maxima per group.
+template <int CB>
+__device__ __forceinline__ void raw_max64_g(const uint32_t (&s)[128], int (&m)[4]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) m[g] = max((int)s[CB + 2 * g], (int)s[CB + 2 * g + 1]);
+#pragma unroll
+  for (int c = 8; c < 64; c += 8) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) m[g] = max(m[g], max((int)s[CB + c + 2 * g], (int)s[CB + c + 2 * g + 1]));
+  }
+}
+// the same over the first n (1..63) columns; a group with no valid column keeps the
+// bits of -inf (a negative integer, below every biased score)
+template <int CB>
+__device__ __forceinline__ void raw_max_ragged_g(uint32_t (&s)[128], int n, int (&m)[4]) {
+  m[0] = (int)s[CB];
+  m[1] = m[2] = m[3] = (int)0xff800000u;
+#pragma unroll
+  for (int c = 1; c < 64; ++c) {
+    if (c < n)
+      m[(c & 7) >> 1] = max(m[(c & 7) >> 1], (int)s[CB + c]);
+    else
+      s[CB + c] = 0xff800000u;
+  }
+}
+
 // P = 2^(S * cc + oo) over columns [CB, CB + 64), written back as floats, on
 // packed fp32 pairs (FFMA2 / FADD2).  Of every 16 columns, 14 take ex2.approx
 // (MUFU) and 2 the polynomial exponential on the FMA pipe (the split measured
 // fastest against 1 in 4, 1 in 16 and none); returns the sum.
-template <int CB>
-__device__ __forceinline__ float exp_block(uint32_t (&s)[128], float cc, float oo) {
-  const float2 c2 = make_float2(cc, cc), o2 = make_float2(oo, oo);
+// KG = 4 (per_thread K scales): pair k of each 8-column chunk is scale group k.
+template <int CB, int KG>
+__device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)[KG], const float (&oo)[KG]) {
+  float2 c2[KG], o2[KG];
+#pragma unroll
+  for (int g = 0; g < KG; ++g) {
+    c2[g] = make_float2(cc[g], cc[g]);
+    o2[g] = make_float2(oo[g], oo[g]);
+  }
   const float2 kM = make_float2(kMagicF, kMagicF), kNM = make_float2(-kMagicF, -kMagicF);
   const float2 kN1 = make_float2(-1.f, -1.f);
   const float2 q0 = make_float2(kP0, kP0), q1 = make_float2(kP1, kP1), q2 = make_float2(kP2, kP2),
@@ -235,7 +282,7 @@ __device__ __forceinline__ float exp_block(uint32_t (&s)[128], float cc, float o
 #pragma unroll
     for (int k = 0; k < 4; ++k)
       x[k] = __ffma2_rn(make_float2(__uint_as_float(s[CB + c + 2 * k]), __uint_as_float(s[CB + c + 2 * k + 1])),
-                        c2, o2);
+                        c2[KG == 1 ? 0 : k], o2[KG == 1 ? 0 : k]);
 #pragma unroll
     for (int k = 0; k < 3; ++k) p[k] = make_float2(ex2(x[k].x), ex2(x[k].y));
     if ((c >> 3) & 1) {
@@ -297,10 +344,10 @@ __device__ __forceinline__ void rebias_s(uint32_t s_addr) {
 // waited for, on pv_done, only before O is rescaled.  P is double-buffered: the
 // buffer written here was last read by the PV of step cnt - 2, which the MMA
 // warp issued before this step's S, so it completed before S did.
-template <int NC>
-__device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint8_t* prow, int r, float c0,
-                                             float c1, int n0, int n1, int cnt, float& m, float& l,
-                                             uint64_t* pv_done, volatile int* abort_flag) {
+template <int NC, int KG>
+__device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint8_t* prow, int r,
+                                             const float (&c0)[KG], const float (&c1)[KG], int n0, int n1, int cnt,
+                                             float& m, float& l, uint64_t* pv_done, volatile int* abort_flag) {
   uint32_t s[128];
   __syncwarp();
   tmem_ld32(s_addr, H3B_S32(s, 0));
@@ -311,13 +358,36 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
     tmem_ld32(s_addr + 64, H3B_S32(s, 64));
     tmem_ld32(s_addr + 96, H3B_S32(s, 96));
   }
-  const int mx0 = n0 == 64 ? raw_max64<0>(s) : raw_max_ragged<0>(s, n0);
-  float tmax = (__int_as_float(mx0) - kMagicF) * c0;
+  float tmax;
+  if constexpr (KG == 1) {
+    const int mx0 = n0 == 64 ? raw_max64<0>(s) : raw_max_ragged<0>(s, n0);
+    tmax = (__int_as_float(mx0) - kMagicF) * c0[0];
+  } else {
+    int mg[4];
+    if (n0 == 64)
+      raw_max64_g<0>(s, mg);
+    else
+      raw_max_ragged_g<0>(s, n0, mg);
+    tmax = fmaxf(fmaxf((__int_as_float(mg[0]) - kMagicF) * c0[0], (__int_as_float(mg[1]) - kMagicF) * c0[1]),
+                 fmaxf((__int_as_float(mg[2]) - kMagicF) * c0[2], (__int_as_float(mg[3]) - kMagicF) * c0[3]));
+  }
   if constexpr (NC == 128) {
     tmem_wait_ld_dep(H3B_S32(s, 64));
     reg_barrier32(H3B_S32(s, 96));
-    const int mx1 = n1 == 64 ? raw_max64<64>(s) : raw_max_ragged<64>(s, n1);
-    tmax = fmaxf(tmax, (__int_as_float(mx1) - kMagicF) * c1);
+    if constexpr (KG == 1) {
+      const int mx1 = n1 == 64 ? raw_max64<64>(s) : raw_max_ragged<64>(s, n1);
+      tmax = fmaxf(tmax, (__int_as_float(mx1) - kMagicF) * c1[0]);
+    } else {
+      int mg[4];
+      if (n1 == 64)
+        raw_max64_g<64>(s, mg);
+      else
+        raw_max_ragged_g<64>(s, n1, mg);
+      tmax = fmaxf(tmax, fmaxf(fmaxf((__int_as_float(mg[0]) - kMagicF) * c1[0],
+                                     (__int_as_float(mg[1]) - kMagicF) * c1[1]),
+                               fmaxf((__int_as_float(mg[2]) - kMagicF) * c1[2],
+                                     (__int_as_float(mg[3]) - kMagicF) * c1[3])));
+    }
   }
   const float m_new = tmax > m + kTau ? tmax : m;
   float alpha = 1.f;
@@ -341,8 +411,16 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
   }
   rebias_s<NC>(s_addr);
   const float off = kLog2_112 - m;
-  float psum = exp_block<0>(s, c0, off - kMagicF * c0);
-  if constexpr (NC == 128) psum += exp_block<64>(s, c1, off - kMagicF * c1);
+  float o0[KG];
+#pragma unroll
+  for (int g = 0; g < KG; ++g) o0[g] = off - kMagicF * c0[g];
+  float psum = exp_block<0, KG>(s, c0, o0);
+  if constexpr (NC == 128) {
+    float o1[KG];
+#pragma unroll
+    for (int g = 0; g < KG; ++g) o1[g] = off - kMagicF * c1[g];
+    psum += exp_block<64, KG>(s, c1, o1);
+  }
   store_p<NC>(s, prow, r);
   tmem_wait_st();
   fence_proxy_async_smem();
@@ -351,6 +429,8 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
   return true;
 }
 
+// KG: K scales per 64-key block (1: per block; 4: Sage per_thread groups)
+template <int KG>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
@@ -539,13 +619,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = quad * 32 + lane;
     const int64_t qrow = (int64_t)(qta + t) * 128 + r;
     const bool row_ok = qrow < a.Lq;
-    const float qs = row_ok ? __ldg(a.q_scale + (int64_t)h * a.nqs + qrow / a.q_block) : 0.f;
+    // Q scale group: q_block rows, or Sage per_thread (rows of equal r % 8 in each 32)
+    const int64_t qsi = a.q_gran ? (qrow >> 5) * 8 + (qrow & 7) : qrow / a.q_block;
+    const float qs = row_ok ? __ldg(a.q_scale + (int64_t)h * a.nqs + qsi) : 0.f;
     const float qsl = qs * a.scale_log2;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + (uint32_t)(t * 128);
     const uint32_t o_addr = tmem + lane_off + 256 + (uint32_t)(t * 128);
     uint8_t* prow0 = smem + kOffP + 2 * t * kPBytes + r * 128;
-    const float* ksc = a.k_scale + (int64_t)h * a.Kb;
+    const float* ksc = a.k_scale + (int64_t)h * a.Kb * KG;
     TileStream ts;
     ts.init(a, h, qta + t, t == 0 || has_b);
     float m = -__int_as_float(0x7f800000), l = 0.f;
@@ -556,10 +638,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // query row or key block, is floored so that masked -inf columns stay -inf)
     int j0, j1;
     bool have = ts.next_pair(j0, j1);
-    float c0 = 0.f, c1 = 0.f;
-    if (have) {
-      c0 = fmaxf(qsl * __ldg(ksc + j0), 1e-30f);
-      c1 = j1 >= 0 ? fmaxf(qsl * __ldg(ksc + j1), 1e-30f) : 0.f;
+    float c0[KG], c1[KG];
+#pragma unroll
+    for (int g = 0; g < KG; ++g) {
+      c0[g] = have ? fmaxf(qsl * __ldg(ksc + (int64_t)j0 * KG + g), 1e-30f) : 0.f;
+      c1[g] = have && j1 >= 0 ? fmaxf(qsl * __ldg(ksc + (int64_t)j1 * KG + g), 1e-30f) : 0.f;
     }
     while (have) {
       const bool two = j1 >= 0;
@@ -567,10 +650,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int n1 = two ? (int)min((int64_t)64, a.Lk - (int64_t)j1 * 64) : 64;
       int nj0, nj1;
       const bool nhave = ts.next_pair(nj0, nj1);
-      float nc0 = 0.f, nc1 = 0.f;
+      float nc0[KG], nc1[KG];
+#pragma unroll
+      for (int g = 0; g < KG; ++g) nc0[g] = nc1[g] = 0.f;
       if (nhave) {
-        nc0 = ld_early(ksc + nj0);
-        nc1 = ld_early(ksc + (nj1 >= 0 ? nj1 : nj0));
+        ld_early_kg<KG>(ksc + (int64_t)nj0 * KG, nc0);
+        ld_early_kg<KG>(ksc + (int64_t)(nj1 >= 0 ? nj1 : nj0) * KG, nc1);
       }
       if (!mbar_wait_warp(&s_full[t], (uint32_t)(cnt & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) {
         ok = false;
@@ -578,18 +663,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       tc_fence_after();
       uint8_t* prow = prow0 + (cnt & 1) * kPBytes;
-      ok = two ? softmax_step<128>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
-                                   abort_flag)
-               : softmax_step<64>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
-                                  abort_flag);
+      ok = two ? softmax_step<128, KG>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
+                                       abort_flag)
+               : softmax_step<64, KG>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
+                                      abort_flag);
       if (!ok) break;
       mbar_arrive(&p_full[t]);
       ++cnt;
       have = nhave;
       j0 = nj0;
       j1 = nj1;
-      c0 = fmaxf(qsl * nc0, 1e-30f);
-      c1 = fmaxf(qsl * nc1, 1e-30f);
+#pragma unroll
+      for (int g = 0; g < KG; ++g) {
+        c0[g] = fmaxf(qsl * nc0[g], 1e-30f);
+        c1[g] = fmaxf(qsl * nc1[g], 1e-30f);
+      }
     }
     // epilogue: O / l * v_scale
     uint16_t* dst = a.out + (row_ok ? qrow : 0) * a.out_stride + (int64_t)h * 128;
@@ -642,16 +730,17 @@ int launch_attention(const void* q, const void* k, const void* vt, const AttnArg
   if (!make_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.Lkpad, (uint64_t)(a.H * 128),
                     (uint64_t)a.Lkpad, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return 1;
+  auto kern = a.k_gran ? attn_kernel<4> : attn_kernel<1>;
   cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, attn_kernel);
+  cudaError_t e = cudaFuncGetAttributes(&fa, kern);
   if (e == cudaSuccess && fa.numRegs != kLaunchRegs) {
     *err = cudaSuccess;
     return 3;  // the register split was planned for a different launch register count
   }
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e == cudaSuccess) {
     dim3 grid((unsigned)(((a.Lq + 127) / 128 + 1) / 2), (unsigned)a.H);
-    attn_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(tq, tk, tv, a);
+    kern<<<grid, kAttnThreads, kAttnSmem, s>>>(tq, tk, tv, a);
     e = cudaGetLastError();
   }
   *err = e;

@@ -260,6 +260,92 @@ cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ Sage per_thread INT8
+
+// Scale groups of Sage's per_thread granularity (qk_quant_gran 3): for Q, 128-row
+// blocks of 32 groups, row r of a block in group (r / 32) * 8 + r % 8; for K, 64-row
+// blocks of 4 groups, row r in group (r % 8) / 2 -- the rows one sm89 MMA thread
+// holds (model/sage_fused_quant.py:41-44 for K; the Q grouping of the grid and scale
+// shape at model/sage_fused_quant.py:201-222).  Per group: scale = max|v|/127 + 1e-7,
+// code = trunc(v / scale + 0.5 sign); K values are bf16(k - mean).
+// One CTA of four warps per (block, head): lane l owns channels 4l..4l+3, warp w the
+// rows w, w+4, ...; each row's values stay in shared memory between the two passes.
+template <int BLK, int NG>
+__device__ __forceinline__ int group_of_row(int r) {
+  return NG == 32 ? (r >> 5) * 8 + (r & 7) : (r & 7) >> 1;
+}
+
+template <int BLK, int NG>
+__global__ void __launch_bounds__(128) quant_per_thread_kernel(PoolArgs a) {
+  __shared__ uint2 rows_s[BLK][32];
+  __shared__ float ramax_s[BLK];
+  __shared__ float gscale_s[NG];
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = (int64_t)b * BLK;
+  const int valid = (int)((a.L - r0) < BLK ? (a.L - r0) : BLK);
+  float mean4[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.mean) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(a.mean + h * kD + 4 * lane);
+    mean4[0] = __uint_as_float(raw.x << 16);
+    mean4[1] = __uint_as_float(raw.x & 0xffff0000u);
+    mean4[2] = __uint_as_float(raw.y << 16);
+    mean4[3] = __uint_as_float(raw.y & 0xffff0000u);
+  }
+#pragma unroll 4
+  for (int r = warp; r < BLK; r += 4) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < valid) load4_row(a, r0 + r, h, lane, mean4, v);
+    rows_s[r][lane] = make_uint2((__float_as_uint(v[0]) >> 16) | (__float_as_uint(v[1]) & 0xffff0000u),
+                                 (__float_as_uint(v[2]) >> 16) | (__float_as_uint(v[3]) & 0xffff0000u));
+    float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    if (lane == 0) ramax_s[r] = am;
+  }
+  __syncthreads();
+  if (threadIdx.x < NG) {
+    const int g = threadIdx.x;
+    float am = 0.f;
+    for (int r = 0; r < BLK; ++r)
+      if (group_of_row<BLK, NG>(r) == g) am = fmaxf(am, ramax_s[r]);
+    const float sc = __fadd_rn(__fdiv_rn(am, 127.0f), 1e-7f);
+    gscale_s[g] = sc;
+    a.scale[(int64_t)h * a.nb_stride + (int64_t)b * NG + g] = sc;
+  }
+  __syncthreads();
+#pragma unroll 4
+  for (int r = warp; r < BLK; r += 4) {
+    uint32_t word = 0;
+    if (r < valid) {
+      const float sc = gscale_s[group_of_row<BLK, NG>(r)];
+      const float rsc = __frcp_rn(sc);
+      const uint2 raw = rows_s[r][lane];
+      const float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                          __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float t = div_rn_by(v[i], sc, rsc);
+        t = __fadd_rn(t, t >= 0.0f ? 0.5f : -0.5f);
+        const int code = __float2int_rz(fminf(127.0f, fmaxf(-127.0f, t)));
+        word |= ((uint32_t)code & 0xffu) << (8 * i);
+      }
+    }
+    *reinterpret_cast<uint32_t*>(a.q + ((int64_t)h * a.Lpad + r0 + r) * kD + 4 * lane) = word;
+  }
+}
+
+cudaError_t launch_quant_per_thread(const PoolArgs& a, int kind, cudaStream_t s) {
+  if (kind == 0) {
+    dim3 grid((unsigned)((a.L + 127) / 128), a.H);
+    quant_per_thread_kernel<128, 32><<<grid, 128, 0, s>>>(a);
+  } else {
+    dim3 grid((unsigned)((a.L + 63) / 64), a.H);
+    quant_per_thread_kernel<64, 4><<<grid, 128, 0, s>>>(a);
+  }
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ q/k RMSNorm + RoPE
 
 // In place on the projection output rows, per (token, q|k, head):

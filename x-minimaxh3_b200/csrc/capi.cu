@@ -271,6 +271,22 @@ int h3b_pool_sim_quant_slab(const void* x, int64_t rows, int64_t H, int64_t x_ro
   return cuda_status(h3b::launch_pool_sim_quant(a, st(stream)), "pool_sim_quant_slab");
 }
 
+int h3b_quantize_per_thread_int8(const void* x, int64_t L, int64_t H, int64_t x_row_stride, const void* mean,
+                                 int kind, void* qi8, void* scale, int64_t Lpad, void* stream) {
+  if (L <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "L and H must be positive");
+  if (!x || !qi8 || !scale) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (kind != 0 && kind != 1) return fail(H3B_ERR_INVALID_ARGUMENT, "kind must be 0 (Q) or 1 (K)");
+  const int blk = kind == 0 ? 128 : 64, ng = kind == 0 ? 32 : 4;
+  const int64_t nb = (L + blk - 1) / blk;
+  if (Lpad < nb * blk) return fail(H3B_ERR_INVALID_ARGUMENT, "Lpad < ceil(L/block)*block");
+  if (x_row_stride < H * 128 || x_row_stride % 4) return fail(H3B_ERR_INVALID_ARGUMENT, "bad x_row_stride");
+  if (nb > INT_MAX || H > 65535) return fail(H3B_ERR_UNSUPPORTED, "too many blocks or heads");
+  h3b::PoolArgs a{static_cast<const uint16_t*>(x), L, x_row_stride, Lpad, (int)H, blk,
+                  static_cast<const uint16_t*>(mean), nullptr, nullptr, nullptr, static_cast<int8_t*>(qi8),
+                  static_cast<float*>(scale), nb * ng};
+  return cuda_status(h3b::launch_quant_per_thread(a, kind, st(stream)), "quantize_per_thread_int8");
+}
+
 int h3b_qk_rmsnorm_rope(void* qkv, int64_t L, int64_t H, int64_t row_stride, int64_t q_offset, int64_t k_offset,
                         const void* q_weight, const void* k_weight, const void* cos_table, const void* sin_table,
                         int rot_dim, float eps, void* stream) {
@@ -338,14 +354,20 @@ int h3b_bitmap_to_lut(const void* bitmap, int64_t rows, int64_t Kb, void* lut, v
   return cuda_status(h3b::launch_bitmap_to_lut(bitmap, rows, Kb, lut, valid, st(stream)), "bitmap_to_lut");
 }
 
-int h3b_attention(const void* q, const void* q_scale, int q_block, int64_t Lq, int64_t Lqpad, const void* k,
-                  const void* k_scale, int64_t Lk, int64_t Lkpad, const void* vt, const void* v_scale, int64_t H,
-                  const void* bitmap, float sm_scale, void* out, int64_t out_row_stride, void* stream) {
+int h3b_attention(const void* q, const void* q_scale, int q_gran, int q_block, int64_t Lq, int64_t Lqpad,
+                  const void* k, const void* k_scale, int k_gran, int64_t Lk, int64_t Lkpad, const void* vt,
+                  const void* v_scale, int64_t H, const void* bitmap, float sm_scale, void* out,
+                  int64_t out_row_stride, void* stream) {
   if (Lq == 0) return ok();
   if (!q || !q_scale || !k || !k_scale || !vt || !v_scale || !out) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
   if (Lq < 0 || Lk <= 0 || H <= 0) return fail(H3B_ERR_INVALID_ARGUMENT, "bad sizes");
+  if (q_gran != 0 && q_gran != 1) return fail(H3B_ERR_INVALID_ARGUMENT, "q_gran must be 0 or 1");
+  if (k_gran != 0 && k_gran != 1) return fail(H3B_ERR_INVALID_ARGUMENT, "k_gran must be 0 or 1");
+  if (q_gran == 1) q_block = 128;
   if (q_block != 32 && q_block != 64 && q_block != 128)
     return fail(H3B_ERR_UNSUPPORTED, "q_block must be 32, 64 or 128");
+  if (k_gran == 1 && (reinterpret_cast<uintptr_t>(k_scale) & 15u))
+    return fail(H3B_ERR_UNSUPPORTED, "per_thread k_scale must be 16-byte aligned");
   if (Lqpad % 128 || Lqpad < Lq || Lkpad % 128 || Lkpad < Lk)
     return fail(H3B_ERR_INVALID_ARGUMENT, "Lqpad / Lkpad must be multiples of 128 covering Lq / Lk");
   if (out_row_stride < H * 128 || out_row_stride % 8) return fail(H3B_ERR_INVALID_ARGUMENT, "bad out_row_stride");
@@ -362,7 +384,9 @@ int h3b_attention(const void* q, const void* q_scale, int q_block, int64_t Lq, i
   a.Kb = (int)((Lk + 63) / 64);
   a.words = (a.Kb + 31) / 32;
   a.q_block = q_block;
-  a.nqs = (int)((Lq + q_block - 1) / q_block);
+  a.q_gran = q_gran;
+  a.k_gran = k_gran;
+  a.nqs = q_gran ? (int)((Lq + 127) / 128 * 32) : (int)((Lq + q_block - 1) / q_block);
   a.q_scale = static_cast<const float*>(q_scale);
   a.k_scale = static_cast<const float*>(k_scale);
   a.v_scale = static_cast<const float*>(v_scale);

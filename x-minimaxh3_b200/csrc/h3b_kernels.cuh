@@ -75,6 +75,9 @@ struct PoolArgs {
   int64_t nb_stride;     // blocks between heads in pooled / similar / scale (0: nb)
 };
 cudaError_t launch_pool_sim_quant(const PoolArgs& a, cudaStream_t s);
+// Sage per_thread INT8: kind 0 Q (128-row blocks, 32 groups), 1 K (64-row blocks,
+// 4 groups); scales at a.scale[h * a.nb_stride + block * groups + g]
+cudaError_t launch_quant_per_thread(const PoolArgs& a, int kind, cudaStream_t s);
 struct QkRopeArgs {
   uint16_t* x;            // bf16 rows [L, stride], q at column q_off, k at k_off (in place)
   int64_t L, stride, q_off, k_off;
@@ -117,6 +120,8 @@ struct AttnArgs {
   int H;
   int64_t Lq, Lqpad, Lk, Lkpad;
   int Kb, words, q_block, nqs;
+  int q_gran;  // 0: q_block-row scale groups; 1: Sage per_thread ((r/32)*8 + r%8)
+  int k_gran;  // 0: one scale per 64-key block; 1: Sage per_thread (4 per block)
   const float* q_scale;
   const float* k_scale;
   const float* v_scale;

@@ -65,6 +65,8 @@ _SIGNATURES = {
     "h3b_key_mean_no_alloc": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "h3b_pool_sim_quant": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p, c_int64, c_void_p],
+    "h3b_quantize_per_thread_int8": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p,
+                                     c_int64, c_void_p],
     "h3b_pool_sim_quant_slab": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_int64, c_int64, c_void_p],
     "h3b_value_fp8_given_absmax": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
@@ -75,8 +77,8 @@ _SIGNATURES = {
     "h3b_block_mask": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                        ctypes.POINTER(MaskParams), c_void_p, c_void_p],
     "h3b_bitmap_to_lut": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
-    "h3b_attention": [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
-                      c_void_p, c_int64, c_void_p, c_float, c_void_p, c_int64, c_void_p],
+    "h3b_attention": [c_void_p, c_void_p, c_int, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64,
+                      c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_float, c_void_p, c_int64, c_void_p],
 }
 _RESTYPES = {"h3b_version": ctypes.c_char_p, "h3b_last_error": ctypes.c_char_p,
              "h3b_key_mean_workspace_bytes": c_int64}

@@ -3,10 +3,10 @@
 Both backends are `AttentionBackend` callables of the native engine
 (model/layers.py:20, 276-300): (q, k, v) bf16 [L, H, 128] -> bf16 [L, H, 128].
 
-* SageAttentionB200    dense: per-block INT8 Q (128 rows) and K (64 rows, K
-                       mean-smoothed), per-channel FP8 V, INT8 QK^T and FP8 PV
-                       on tcgen05 (replaces sage_attention_sm89,
-                       model/kernels.py:7645-7661)
+* SageAttentionB200    dense: INT8 Q and K (K mean-smoothed) in Sage's per_thread,
+                       per_warp or per-block scale groups, per-channel FP8 V,
+                       INT8 QK^T and FP8 PV on tcgen05 (replaces
+                       sage_attention_sm89, model/kernels.py:7645-7746)
 * SpargeAttentionB200  the same kernel driven by the Sparge block mask: pooled
                        similarity, fixed Top-K or top-CDF selection and the
                        mandatory rails (replaces the Sparge backends,
@@ -47,17 +47,24 @@ def _nhd_rows(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
     return x, x.shape[0], x.shape[1], x.stride(0)
 
 
+GRAN_BLOCK, GRAN_PER_THREAD = 0, 1
+
+
 @dataclass
 class PreparedBlocks:
-    """Per-block INT8 tokens with Sparge pooled metadata."""
+    """INT8 tokens with their scales (and, for Sparge, pooled metadata).
 
-    pooled: torch.Tensor    # bf16 [H, nb, 128]
-    similar: torch.Tensor   # u8 [H, nb]
-    qi8: torch.Tensor       # int8 [H, Lpad, 128]
-    scale: torch.Tensor     # f32 [H, nb]
+    gran GRAN_BLOCK: one scale per `block` rows (Sparge per-block, Sage per_warp);
+    gran GRAN_PER_THREAD: Sage per_thread groups (Q: 32 per 128 rows, K: 4 per 64)."""
+
+    pooled: torch.Tensor | None    # bf16 [H, nb, 128] (None: not pooled)
+    similar: torch.Tensor | None   # u8 [H, nb]
+    qi8: torch.Tensor              # int8 [H, Lpad, 128]
+    scale: torch.Tensor            # f32 [H, nb] (per_thread: [H, nb * groups])
     tokens: int
     block: int
     padded: int
+    gran: int = GRAN_BLOCK
 
 
 @dataclass
@@ -108,6 +115,28 @@ def prepare_blocks(x: torch.Tensor, block: int, threshold=-0.1, mean: torch.Tens
     check(lib().h3b_pool_sim_quant(_p(x), L, H, stride, _p(m), block, _p(thr), _p(pooled), _p(similar), _p(qi8),
                                    _p(scale), Lpad, _stream(x)), "pool_sim_quant")
     return PreparedBlocks(pooled, similar, qi8, scale, L, block, Lpad)
+
+
+def quantize_per_thread(x: torch.Tensor, kind: str, mean: torch.Tensor | None = None) -> PreparedBlocks:
+    """Sage per_thread INT8 (qk_quant_gran 3) of Q (kind "q": 32 scale groups per
+    128 rows) or K (kind "k": 4 groups per 64 rows, values bf16(k - mean)); the
+    grouping of sageattention's per_thread_int8 (model/sage_fused_quant.py:20-283)."""
+    _cuda("quantize_per_thread", x, mean)
+    x, L, H, stride = _nhd_rows(x)
+    blk, ng = (128, 32) if kind == "q" else (64, 4)
+    if kind not in ("q", "k"):
+        raise ValueError("kind must be 'q' or 'k'")
+    nb = (L + blk - 1) // blk
+    Lpad = _pad(L)
+    dev = x.device
+    qi8 = torch.empty((H, Lpad, HEAD_DIM), device=dev, dtype=torch.int8)
+    if Lpad > nb * blk:
+        qi8[:, nb * blk:].zero_()
+    scale = torch.empty((H, nb * ng), device=dev, dtype=torch.float32)
+    m = None if mean is None else mean.to(torch.bfloat16).contiguous()
+    check(lib().h3b_quantize_per_thread_int8(_p(x), L, H, stride, _p(m), 0 if kind == "q" else 1, _p(qi8), _p(scale),
+                                             Lpad, _stream(x)), "quantize_per_thread_int8")
+    return PreparedBlocks(None, None, qi8, scale, L, blk, Lpad, GRAN_PER_THREAD)
 
 
 def prepare_queries(q: torch.Tensor, block: int = 128, threshold=-0.1) -> PreparedBlocks:
@@ -215,9 +244,11 @@ def attention(pq: PreparedBlocks, pk: PreparedBlocks, pv: PreparedValues, bitmap
     if out.stride(2) != 1 or out.stride(1) != HEAD_DIM:
         raise ValueError("output must be [Lq, H, 128] with contiguous heads")
     scale = (1.0 / math.sqrt(HEAD_DIM)) if sm_scale is None else float(sm_scale)
-    check(lib().h3b_attention(_p(pq.qi8), _p(pq.scale), pq.block, Lq, pq.padded, _p(pk.qi8), _p(pk.scale), Lk,
-                              pk.padded, _p(pv.vt), _p(pv.scale), H, _p(bitmap), scale, _p(out), out.stride(0),
-                              _stream(out)), "attention")
+    if bitmap is not None and (pq.gran != GRAN_BLOCK or pq.block != 128):
+        raise ValueError("the block mask is defined over 128-row per-block query tiles")
+    check(lib().h3b_attention(_p(pq.qi8), _p(pq.scale), pq.gran, pq.block, Lq, pq.padded, _p(pk.qi8), _p(pk.scale),
+                              pk.gran, Lk, pk.padded, _p(pv.vt), _p(pv.scale), H, _p(bitmap), scale, _p(out),
+                              out.stride(0), _stream(out)), "attention")
     return out
 
 
@@ -257,25 +288,51 @@ class SpargeAttentionB200:
         return attention(pq, pk, pv, bitmap)
 
 
-class SageAttentionB200:
-    """Dense quantized attention backend (q, k, v: bf16 [L, H, 128]).
+QK_QUANT_GRANS = ("per_thread", "per_warp", "per_block")
 
-    q_block: rows per Q scale -- 128 (Sparge per-block), 64 (per-64-token blocks) or
-    32 (Sage's per_warp groups, model/kernels.py:5571-5573).  K: per-64-row blocks
-    after mean smoothing."""
+
+class SageAttentionB200:
+    """Dense quantized attention backend (q, k, v: bf16 [L, H, 128]), the role of
+    sage_attention_sm89 (model/kernels.py:7645-7661) with its qk_quant_gran:
+
+    * "per_thread" (the reference's default, kernels.py:118-120): Q scale groups of 4
+      rows, K groups of 16 keys per 64-key block (quantize_per_thread);
+    * "per_warp": Q groups of 32 rows, K per 64-key block (kernels.py:4142-4151);
+    * "per_block": Q groups of `q_block` rows (128, or 64 for per-64-token blocks),
+      K per 64-key block -- Sparge's per-block quantization.
+
+    K is mean-smoothed (bf16(k - mean_L(k))) unless smooth_k is False; V is per-channel
+    FP8 with scale absmax / 2.25."""
 
     approximate = True
 
-    def __init__(self, q_block: int = 128, smooth_k: bool = True) -> None:
+    def __init__(self, q_block: int = 128, smooth_k: bool = True, qk_quant_gran: str | None = None) -> None:
+        if qk_quant_gran is None:
+            qk_quant_gran = "per_warp" if q_block == 32 else "per_block"
+        if qk_quant_gran not in QK_QUANT_GRANS:
+            raise ValueError(f"qk_quant_gran must be one of {QK_QUANT_GRANS}")
+        if qk_quant_gran == "per_warp":
+            q_block = 32
         if q_block not in (32, 64, 128):
             raise ValueError("q_block must be 32, 64 or 128")
         self.q_block = q_block
+        self.qk_quant_gran = qk_quant_gran
         self.smooth_k = smooth_k
+
+    def quantize_queries(self, q: torch.Tensor) -> PreparedBlocks:
+        if self.qk_quant_gran == "per_thread":
+            return quantize_per_thread(q, "q")
+        return prepare_queries(q, self.q_block)
+
+    def quantize_keys(self, k: torch.Tensor) -> PreparedBlocks:
+        if self.qk_quant_gran == "per_thread":
+            return quantize_per_thread(k, "k", key_mean(k) if self.smooth_k else None)
+        return prepare_keys(k, smooth=self.smooth_k)[0]
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         pv = prepare_values(v)
-        pk, _ = prepare_keys(k, smooth=self.smooth_k)
-        pq = prepare_queries(q, self.q_block)
+        pk = self.quantize_keys(k)
+        pq = self.quantize_queries(q)
         return attention(pq, pk, pv)
 
 
@@ -508,7 +565,7 @@ class DenseLongSequenceB200(_LongSequenceMixin, SageAttentionB200):
     chunk, prefix or video, runs with per-warp Q scales over all keys."""
 
     def __init__(self, smooth_k: bool = True) -> None:
-        super().__init__(q_block=32, smooth_k=smooth_k)
+        super().__init__(smooth_k=smooth_k, qk_quant_gran="per_warp")
 
     def long_sequence_all_queries(self, query: torch.Tensor, prepared: PreparedLongSequenceKVB200) -> torch.Tensor:
         """Every query of the packed sequence, in chunks from its origin (model/layers.py:852-860)."""
