@@ -3,14 +3,16 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl h3b|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: Ulysses)
 
-A step is one forward of one DiT block over the whole 720p/5 s sequence:
+A step is one forward of one DiT block (--layers blocks) over the whole 720p/5 s sequence:
 rms_adaln + ConvRot INT8 quant, INT8 QKV GEMM, q/k RMSNorm + 3-D RoPE, Sparge
 mask (top-CDF 0.6 + first column + diagonal) and quantized attention, INT8
 out-projection with gated residual, W4A8 FC1 (G=128) -> GELU-tanh + ConvRot INT8
 quant -> W4A8 FC2 with gated residual.  Random-init weights, synthetic N(0,1)
-hidden states.  With N GPUs the sequence is split into N token slices (strong
-scaling: total work fixed), GEMMs run on local rows with no communication and
-attention uses a NCCL all-to-all (tokens -> heads and back).
+hidden states from one seed.  With N GPUs the sequence is split into N token
+slices (strong scaling: total work fixed, every N times identical inputs and
+masks), GEMMs run on local rows with no communication and attention uses NCCL
+all-to-alls (tokens -> heads as three async exchanges of K, V, Q; heads ->
+tokens), with heads assigned to ranks by the first warm-up step's kept tiles.
 
 Prints ONE JSON line on rank 0 (see the keys below).  `value` is device-timed
 with inputs resident in HBM; `e2e` adds the pinned host->device copy of each
@@ -51,6 +53,7 @@ def parse():
     ap.add_argument("--tokens", type=int, default=0, help="override L (must divide by the GPU count)")
     ap.add_argument("--grid", type=str, default="", help="latent video grid T,H,W (default 31,45,80 = 720p/5 s; "
                     "91,68,120 = 1080p/15 s); L is its product unless --tokens is given")
+    ap.add_argument("--layers", type=int, default=1, help="DiT blocks per step (BASELINE config 5: 4)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", type=str, default="",
@@ -86,22 +89,30 @@ def run_reference(args, L):
 
     torch.set_num_threads(os.cpu_count() or 1)
     block = R.ReferenceBlockCPU()
-    vals = []
+    vals, walls = [], []
     info = None
     for i in range(args.warmup + args.steps):
         info = R.measure(L=L, row_sample=512, query_sample=512, block=block, seed=i)
         if i >= args.warmup:
-            vals.append(info["seconds_per_block"])
+            vals.append(info["seconds_per_block"] * args.layers)
+            walls.append(info["sample_seconds"])
     sec = sorted(vals)[len(vals) // 2]
+    wall = sorted(walls)[len(walls) // 2]
     value = L / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000.0, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32 (dequantized weights, torch CPU)",
-        "data": "synthetic", "config": {"workload": workload_name(args.grid_t), "tokens": L,
-                                         "hidden": 4096, "heads": 32, "ffn": 16384, "attention": "dense SDPA (CPU)"},
+        "steps": args.steps, "warmup": args.warmup,
+        # what each timed step actually ran: one bounded sample (see cpu_baseline.sample)
+        "ms_per_step": wall * 1000.0,
+        "extrapolated": {"ms_per_block_step": sec * 1000.0,
+                         "how": "value = tokens / (the sample's time extrapolated to the whole block)"},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (dequantized weights, torch CPU)", "data": "synthetic",
+        "config": {"workload": workload_name(args.grid_t), "tokens": L, "layers": args.layers, "hidden": 4096,
+                   "heads": 32, "ffn": 16384,
+                   "attention": "dense torch SDPA (the reference's CPU attention; the B200 arm runs Sparge)"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info["threads"], "kind": "port",
-                         "sample": info["sample"] + "; median of the timed steps"},
+                         "sample": info["sample"] + f"; median of {args.steps} timed samples ({R.cpu_model()})"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -400,10 +411,14 @@ def run_h3b(args, L):
         raise SystemExit(f"{L} tokens do not split over {world} ranks")
     Lp = L // world
     cfg = BlockConfig()
-    block = DiTBlockB200(cfg, device=dev, seed=0, group=group)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    x0 = torch.randn(Lp, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    blocks = [DiTBlockB200(cfg, device=dev, seed=layer, group=group) for layer in range(args.layers)]
+    # one global input from one seed, each rank taking its own token rows: every N times
+    # the same work and the same masks
+    g = torch.Generator(device=dev).manual_seed(1234)
+    x_full = torch.randn(L, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
     t = torch.randn(cfg.t_dim, generator=g, device=dev).to(torch.bfloat16)
+    x0 = x_full[rank * Lp:(rank + 1) * Lp].clone()
+    del x_full
     rope = rope_tables(args.grid_t, cfg.rope_splits, start=rank * Lp, count=Lp, device=dev)
     x = torch.empty_like(x0)
 
@@ -427,14 +442,20 @@ def run_h3b(args, L):
 
     def step():
         x.copy_(x0)
-        block.forward(x, t, rope)
+        for blk in blocks:
+            blk.forward(x, t, rope)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
         step()
+        if i == 0 and world > 1:
+            # assign heads to ranks by the kept tiles the first step measured (the
+            # blocks' outputs do not depend on the assignment)
+            for blk in blocks:
+                blk.rebalance_heads()
     torch.cuda.synchronize()
     barrier()
     attn_events.clear()
@@ -458,12 +479,18 @@ def run_h3b(args, L):
     launches = _lib.launch_count()
     ms = s_ev.elapsed_time(e_ev) / args.steps
     attn_ms = sum(a.elapsed_time(b) for a, b in attn_events) / max(1, len(attn_events))
-    pq, pk, pv, bitmap = block._last_attn
-    attn_ops_launch = attention_ops(bitmap, pq.tokens, pk.tokens, pq.qi8.shape[0])
+    # executed tensor ops of one attention launch (this rank's heads), averaged over layers
+    attn_ops_launch = sum(attention_ops(b._last_attn[3], b._last_attn[0].tokens, b._last_attn[1].tokens,
+                                        b._last_attn[0].qi8.shape[0]) for b in blocks) / len(blocks)
+    pq0, pk0 = blocks[0]._last_attn[0], blocks[0]._last_attn[1]
+    rank_attn = None
     if world > 1:
         tmax = torch.tensor([ms, attn_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        ms, attn_ms = float(tmax[0]), float(tmax[1])
+        per = [torch.zeros(2, device=dev, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(per, torch.tensor([attn_ms, attn_ops_launch], device=dev, dtype=torch.float64))
+        rank_attn = [(float(p[0]), float(p[1])) for p in per]
+        ms = float(tmax[0])
     status = h3b.device_status(local)
 
     # end-to-end through the public host-side runner (h3b.block.HostPipeline):
@@ -471,12 +498,12 @@ def run_h3b(args, L):
     # runs the block and copies the result back; the copies of neighbouring
     # steps overlap the block on their own streams
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and args.layers == 1:
         from h3b.block import HostPipeline
         xh = x0.cpu().pin_memory()
         th = t.cpu().pin_memory()
         outs = [torch.empty_like(xh).pin_memory() for _ in range(2)]
-        pipe = HostPipeline(block, rope, Lp)
+        pipe = HostPipeline(blocks[0], rope, Lp)
         pipe.run([xh] * 2, [th] * 2, outs)                      # warm-up
         torch.cuda.synchronize()
         barrier()
@@ -508,14 +535,14 @@ def run_h3b(args, L):
         info = None
         while time.time() < t_end or not samples:
             info = R.measure(L=L, row_sample=512, query_sample=512, block=rb, seed=len(samples))
-            samples.append(info["seconds_per_block"])
+            samples.append(info["seconds_per_block"] * args.layers)
         sec = sorted(samples)[len(samples) // 2]
         cpu = {"value": L / sec, "unit": "tokens/s", "cores": info["threads"], "kind": "port",
                "sample": info["sample"] + f"; median of {len(samples)} samples ({R.cpu_model()})"}
 
     if rank == 0:
         peaks, src = measured_peaks()
-        peak = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
+        peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
         achieved = attn_ops_launch / (attn_ms / 1000.0) / 1e12
         traffic = None
         prof = os.path.join(ROOT, "profiles", "attn_traffic.json")
@@ -527,28 +554,35 @@ def run_h3b(args, L):
                     traffic = prof_d.get("bytes_per_launch_scaled")
             except (OSError, ValueError):
                 traffic = None
-        density = attn_ops_launch / (4.0 * 128 * 64 * 128 * math.ceil(pq.tokens / 128) * math.ceil(pk.tokens / 64)
-                                     * pq.qi8.shape[0])
+        heads_local = pq0.qi8.shape[0]
+        dense_ops = 4.0 * 128 * 64 * 128 * math.ceil(pq0.tokens / 128) * math.ceil(pk0.tokens / 64) * heads_local
+        density = attn_ops_launch / dense_ops
         line = {
             "metric": METRIC, "value": L / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 (W8A8 / W4A8 GEMMs), int8-QK / fp8-PV attention",
-            "data": "synthetic (N(0,1) hidden states, random-init H3-format weights)",
+            "data": "synthetic (N(0,1) hidden states from one seed, each rank its token rows; random-init "
+                    "H3-format weights)",
             "config": {"workload": workload_name(args.grid_t) + " (BASELINE configs 1-4 combined in one block)",
-                       "tokens": L, "grid": list(args.grid_t), "hidden": cfg.hidden, "heads": cfg.heads,
-                       "ffn": cfg.ffn, "mlp": f"W4A8 G={cfg.w4_group} {cfg.mlp_act}",
+                       "tokens": L, "layers": args.layers, "grid": list(args.grid_t), "hidden": cfg.hidden,
+                       "heads": cfg.heads, "ffn": cfg.ffn, "mlp": f"W4A8 G={cfg.w4_group} {cfg.mlp_act}",
                        "attention": f"Sparge {cfg.mask.mode} {cfg.mask.budget} + first column + diagonal",
                        "kept_tile_fraction": round(density, 4),
                        "parallelism": f"ulysses{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (hidden 914 MB, weights 33-100 MB per layer)"},
             "roofline": {"bound": "tensor", "kernel": "h3b attn_kernel (tcgen05 int8 QK + fp8 PV)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": f"2 x bf16_tflops_sustained of {src} (int8/fp8 dense rate is twice bf16)",
-                         "traffic": traffic, "attn_ms_per_launch": attn_ms,
-                         "ops_per_launch": attn_ops_launch},
+                         "peak_source": f"2 x bf16_tflops (burst) of {src} (int8/fp8 dense rate is twice bf16)",
+                         "traffic": traffic, "attn_ms_per_launch": attn_ms, "ops_per_launch": attn_ops_launch},
             "gpu_launches": launches,
             "device_status": status,
         }
+        if rank_attn:
+            times = [a for a, _ in rank_attn]
+            line["ranks"] = {"attn_ms_per_launch": [round(a, 3) for a in times],
+                             "attn_ops_per_launch": [o for _, o in rank_attn],
+                             "attn_max_over_mean": max(times) / (sum(times) / len(times)),
+                             "head_assignment": "balanced by the kept tiles of the first warm-up step"}
         if e2e:
             line["e2e"] = e2e
         if cpu:

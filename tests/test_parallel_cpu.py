@@ -79,6 +79,33 @@ def exchange_roundtrip(rank, world):
     return True
 
 
+def async_exchange_with_order(rank, world):
+    """K, V, Q exchanged separately with a head order that sends heads out of order:
+    each rank receives exactly its assigned heads of every token, the output exchange
+    restores head index order, and the balanced assignment is identical on both ranks."""
+    from h3b import parallel as P
+    L, H, D = 12, 4, 8
+    full = _full_qkv(L, H, D)
+    r0, n = P.shard_rows(L, world, rank)
+    local = full[r0:r0 + n].clone()
+    order = torch.tensor([3, 0, 2, 1])
+    ex = P.exchange_qkv_async(local, H, D, order=order)
+    mine = order[rank * 2:(rank + 1) * 2]
+    view = full.view(L, 3, H, D)
+    for name, slot in (("k", 1), ("v", 2), ("q", 0)):
+        t, work = ex[name]
+        work.wait()
+        assert torch.equal(t, view[:, slot][:, mine]), name
+    q, _ = ex["q"]
+    back = P.heads_to_tokens(q.reshape(L, 2 * D), n, order=order)
+    assert torch.equal(back, full[r0:r0 + n, :H * D])
+    counts = P.gather_head_counts(torch.tensor([10.0 * rank + 1, 10.0 * rank + 2]), order, H)
+    expect = torch.empty(4)
+    expect[order] = torch.tensor([1.0, 2.0, 11.0, 12.0])
+    assert torch.equal(counts, expect)
+    return P.balanced_head_order(counts, world).tolist()
+
+
 def dead_peer(rank, world):
     import torch.distributed as dist
     from h3b import parallel as P
@@ -99,6 +126,26 @@ def test_shard_rows():
 def test_ulysses_exchange_roundtrip_gloo():
     out = _run(exchange_roundtrip)
     assert out[0] == ("ok", True) and out[1] == ("ok", True), out
+
+
+def test_async_exchange_with_head_order_gloo():
+    out = _run(async_exchange_with_order)
+    assert out[0][0] == "ok" and out[1][0] == "ok", out
+    assert out[0][1] == out[1][1]                     # both ranks choose the same assignment
+
+
+def test_balanced_head_order():
+    from h3b import parallel as P
+    kept = torch.tensor([900, 100, 120, 880, 500, 510, 300, 290, 50, 60, 700, 650, 410, 420, 330, 340])
+    for world in (2, 4, 8):
+        order = P.balanced_head_order(kept, world)
+        assert sorted(order.tolist()) == list(range(16))
+        load = kept[order].view(world, -1).sum(1).double()
+        naive = kept.view(world, -1).sum(1).double()
+        assert load.max() / load.mean() <= naive.max() / naive.mean()
+        # the heaviest head (900) needs a partner of at least 50 when each rank takes two
+        best = {2: 3280, 4: 1640, 8: 950}[world]
+        assert load.max() <= best * 1.02
 
 
 def test_dead_rank_surfaces_as_error():

@@ -6,7 +6,8 @@ Per block (model/layers.py:1074-1298, fused_mlp.py:269-426):
   qkv = INT8 GEMM(xq, W_qkv) + bias, with    h3b_int8_gemm_dequant_qk_rope (one kernel;
     q, k <- per-head RMSNorm + 3-D RoPE       h3b_int8_gemm_dequant + h3b_qk_rmsnorm_rope
     in the epilogue                           for shapes the fused epilogue does not take)
-  [Ulysses all-to-all tokens -> heads]        NCCL, only when world > 1
+  [Ulysses all-to-all tokens -> heads]        NCCL, only when world > 1: K, V, Q as
+                                              three async exchanges overlapping the K / V prep
   attention (Sparge-masked quantized)         prep / mask / h3b_attention
   [all-to-all heads -> tokens]
   x += gate_a * INT8 GEMM(ConvRot INT8(o))    h3b_quantize_int8_rowwise_convrot + gated-residual GEMM
@@ -173,6 +174,7 @@ class DiTBlockB200:
         if cfg.heads % self.world:
             raise ValueError(f"{cfg.heads} heads do not split over {self.world} ranks")
         self.last_mask_density: float | None = None
+        self.head_order: torch.Tensor | None = None   # Ulysses head -> rank assignment (None: in order)
 
     @classmethod
     def from_parts(cls, cfg: BlockConfig, *, ada_w, ada_b, norm1, norm2, q_norm, k_norm, qkv, out, fc1, fc2,
@@ -221,6 +223,42 @@ class DiTBlockB200:
         self._last_attn = (pq, pk, pv, bitmap)
         return A.attention(pq, pk, pv, bitmap)
 
+    def attention_ulysses(self, qkv: torch.Tensor) -> torch.Tensor:
+        """qkv: this rank's token rows [L/P, 3*H*128] -> o [L, H/P, 128] for this rank's
+        heads.  K, V and Q cross NVLink as three asynchronous all-to-alls; the K
+        preparation starts when K has arrived, while V and Q are still in flight."""
+        cfg = self.cfg
+        ex = P.exchange_qkv_async(qkv, cfg.heads, cfg.head_dim, self.group, self.head_order)
+        k, work = ex["k"]
+        work.wait()
+        pk, _ = A.prepare_keys(k)
+        v, work = ex["v"]
+        work.wait()
+        pv = A.prepare_values(v)
+        q, work = ex["q"]
+        work.wait()
+        pq = A.prepare_queries(q)
+        bitmap = A.block_mask(pq, pk, cfg.mask) if cfg.mask is not None else None
+        self._last_attn = (pq, pk, pv, bitmap)
+        return A.attention(pq, pk, pv, bitmap)
+
+    def rebalance_heads(self) -> torch.Tensor | None:
+        """Reassign heads to ranks so each rank's Sparge work (kept tiles of the last
+        forward) is nearly equal; every rank computes the same order.  Collective:
+        call on all ranks between forwards.  The block's output does not depend on
+        the assignment."""
+        if self.world == 1 or getattr(self, "_last_attn", None) is None:
+            return self.head_order
+        pq, pk, _, bitmap = self._last_attn
+        hl = pq.qi8.shape[0]
+        if bitmap is None:
+            local = torch.full((hl,), float(pq.qi8.shape[1] // 128), device=self.device)
+        else:
+            local = kept_tiles_per_head(bitmap).to(torch.float64)
+        counts = P.gather_head_counts(local, self.head_order, self.cfg.heads, self.group)
+        self.head_order = P.balanced_head_order(counts, self.world)
+        return self.head_order
+
     @staticmethod
     def _gated(lin, x, gate, q, s, runs) -> None:
         if runs is None:
@@ -260,8 +298,8 @@ class DiTBlockB200:
             self.qkv.forward_prequantized_qk_rope(xq, xs, qkv[r0:r1], cfg.heads, 0, W, self.q_norm, self.k_norm,
                                                   rope[0][r0:r1], rope[1][r0:r1], cfg.qk_eps)
         if self.world > 1:
-            o = self.attention(P.tokens_to_heads(qkv, cfg.heads, cfg.head_dim, self.group))
-            o2 = P.heads_to_tokens(o.view(o.shape[0], -1), Lp, self.group)
+            o = self.attention_ulysses(qkv)
+            o2 = P.heads_to_tokens(o.view(o.shape[0], -1), Lp, self.group, self.head_order)
         else:
             o2 = self.attention(qkv).view(Lp, W)
         del qkv
@@ -389,6 +427,16 @@ class HostPipeline:
             else:
                 read_out[b] = store(k, 0, whole[1])
         comp.wait_stream(self.s_out)
+
+
+def kept_tiles_per_head(bitmap: torch.Tensor) -> torch.Tensor:
+    """Kept (Q block, K block) tiles of each head, int64 [H] on the bitmap's device."""
+    v = bitmap.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    cnt = torch.zeros(v.shape[0], dtype=torch.int64, device=v.device)
+    for _ in range(32):
+        cnt += (v & 1).sum(dim=(1, 2))
+        v = v >> 1
+    return cnt
 
 
 def kept_tiles(bitmap: torch.Tensor, key_tokens: int) -> int:
