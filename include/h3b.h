@@ -144,6 +144,24 @@ int h3b_dequant_int4_grouped_to_int8(const void* qweight, const void* s_rel, int
                                      const void* codebook, void* out, int64_t N, int64_t K, int64_t G,
                                      void* stream);
 
+/* The activations of the W4A8 group correction (asymmetric int4 weights carry a
+ * per-group offset, applied as out += sx @ correction): sx[m, g] = bf16(bf16(sum of
+ * the G codes xq[m, g*G .. g*G+G-1]) * bf16(xs[m])) for g < K/G; columns [K/G,
+ * sx_row_stride) are written 0.  xq: int8 [M, K] (the linear's quantized input),
+ * xs: f32 [M]; sx: bf16 [M, sx_row_stride].  Replaces the eager group sum of
+ * comfy_kitchen backends/cuda/__init__.py:2294-2296. */
+int h3b_w4a8_group_sums(const void* xq, const void* xs, int64_t M, int64_t K, int64_t G, void* sx,
+                        int64_t sx_row_stride, void* stream);
+
+/* D[m, n] = bf16(float(D[m, n]) + sum_k A[m, k] * B[n, k]) on tcgen05 (kind::f16,
+ * bf16 operands, fp32 accumulation in tensor memory), in place.  A: bf16 [M, K],
+ * B: bf16 [N, K] (both rows of K contiguous, K % 8 == 0), D: bf16 with row stride
+ * out_row_stride (even).  With A = the group sums above and B = correction^T this is
+ * the W4A8 group correction; replaces out.addmm_(sx, correction) (comfy_kitchen
+ * backends/cuda/__init__.py:2297). */
+int h3b_bf16_gemm_accumulate(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
+                             int64_t out_row_stride, void* stream);
+
 /* ---------------------------------------------------------------- attention preparation */
 
 /* Bytes of workspace h3b_key_mean needs for L tokens and H heads. */

@@ -826,6 +826,31 @@ void h3bo_attention(const int8_t* q, const float* qscale, int qblk, int64_t Lq, 
     }
 }
 
+/* W4A8 group correction (comfy_kitchen backends/cuda/__init__.py:2294-2297):
+ *   sx[m, g] = bf16(bf16(sum of the G codes of group g) * bf16(xs[m]))
+ *   out[m, n] = bf16(float(out[m, n]) + sum_g sx[m, g] * corr[g, n])
+ * corr: bf16 bits [K/G, N]; the sum over groups in double (the GPU accumulates the
+ * exact bf16 products in fp32 inside the tensor core). */
+void h3bo_w4a8_correction(const int8_t* xq, const float* xs, int64_t M, int64_t K, int64_t G,
+                          const uint16_t* corr, int64_t N, uint16_t* out) {
+    const int64_t groups = K / G;
+    float* sx = (float*)malloc(sizeof(float) * (size_t)groups);
+    for (int64_t m = 0; m < M; ++m) {
+        const float xb = bf16r(xs[m]);
+        for (int64_t g = 0; g < groups; ++g) {
+            int32_t sum = 0;
+            for (int64_t k = 0; k < G; ++k) sum += xq[m * K + g * G + k];
+            sx[g] = bf16r(bf16r((float)sum) * xb);
+        }
+        for (int64_t n = 0; n < N; ++n) {
+            double dot = 0.0;
+            for (int64_t g = 0; g < groups; ++g) dot += (double)sx[g] * (double)bf16_to_f32(corr[g * N + n]);
+            out[m * N + n] = f32_to_bf16(bf16_to_f32(out[m * N + n]) + (float)dot);
+        }
+    }
+    free(sx);
+}
+
 /* ------------------------------------------------------------------------- */
 /* Quantized attention with the kernel's own P arithmetic                    */
 /* ------------------------------------------------------------------------- */

@@ -336,3 +336,15 @@ def quant_per_thread(x_bf16, kind: int, mean=None):
     lib().h3bo_quant_per_thread(_p(x), I64(L), I64(H), _p(_c(mean, np.uint16)), ctypes.c_int(kind), _p(q),
                                 I64(Lpad), _p(sc))
     return q, sc
+
+
+def w4a8_correction(xq, xs, G: int, corr_bf16, out_bf16):
+    """The W4A8 group correction added into out (h3bo_w4a8_correction); returns new bits."""
+    xq = _c(xq, np.int8)
+    M, K = xq.shape
+    corr = _c(corr_bf16, np.uint16)
+    N = corr.shape[1]
+    out = np.array(out_bf16, dtype=np.uint16, copy=True)
+    lib().h3bo_w4a8_correction(_p(xq), _p(_c(xs, np.float32).reshape(-1)), I64(M), I64(K), I64(G), _p(corr), I64(N),
+                               _p(out))
+    return out

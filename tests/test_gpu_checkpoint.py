@@ -65,6 +65,11 @@ def test_layers_match_oracle_and_engine(env):
             corr = plain.clone()
             ops.w4a8_group_correction_(corr, xq, xs, lin.correction, lin.spec.group_size)
             assert torch.equal(corr, out), tag
+            # the native correction against the oracle's: within one bf16 ulp
+            exp = O.w4a8_correction(xq.cpu().numpy(), xs.cpu().numpy(), lin.spec.group_size,
+                                    bits(lin.correction.to(torch.bfloat16)), bits(plain))
+            diff = np.abs(bits(out).astype(np.int32) - exp.astype(np.int32))
+            assert diff.max() <= 1, tag
 
 
 def test_block_from_safetensors_tracks_engine_block(env, tmp_path):

@@ -284,3 +284,35 @@ def test_module_injection_matches_reference_module(ops):
 def test_no_device_timeouts_recorded(ops):
     from h3b import device_status
     assert device_status(0) == 0
+
+
+def _bf16_ulps(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """|a - b| in bf16 units in the last place (bit patterns, sign-magnitude)."""
+    def key(x):
+        x = x.astype(np.int32)
+        return np.where(x & 0x8000, -(x & 0x7FFF), x & 0x7FFF)
+    return np.abs(key(a) - key(b))
+
+
+@pytest.mark.parametrize("m,k,g,n", [(300, 5376, 16, 1000), (4096, 14336, 16, 5376), (129, 2048, 4, 520),
+                                     (64, 4096, 128, 4096)])
+def test_w4a8_group_correction_native(ops, m, k, g, n):
+    """The W4A8 group correction (comfy_kitchen backends/cuda/__init__.py:2294-2297) as two
+    native kernels (group sums, then a tcgen05 bf16 GEMM accumulating into the output):
+    within one bf16 ulp of the oracle (which sums the exact bf16 products in double) on
+    every element, and of the reference's own formula (torch addmm on the GPU)."""
+    gen = torch.Generator().manual_seed(m + k + n)
+    xq = torch.randint(-127, 128, (m, k), generator=gen, dtype=torch.int16).to(torch.int8)
+    xs = torch.rand(m, generator=gen) * 1e-2 + 1e-4
+    corr = (torch.randn(k // g, n, generator=gen) * 0.02).to(torch.bfloat16)
+    out0 = torch.randn(m, n, generator=gen).to(torch.bfloat16)
+    out = out0.cuda()
+    ops.w4a8_group_correction_(out, xq.cuda(), xs.cuda(), corr.cuda(), g)
+    exp = O.w4a8_correction(xq.numpy(), xs.numpy(), g, bits(corr), bits(out0))
+    ulps = _bf16_ulps(bits(out), exp)
+    assert ulps.max() <= 1 and (ulps == 0).mean() >= 0.99, (ulps.max(), (ulps == 0).mean())
+    # the reference's eager formula, on the GPU (cuBLAS)
+    sx = xq.cuda().view(m, k // g, g).sum(-1, dtype=torch.int32).to(torch.bfloat16)
+    sx = sx * xs.cuda().to(torch.bfloat16)
+    ref = out0.cuda().addmm_(sx, corr.cuda())
+    assert _bf16_ulps(bits(out), bits(ref)).max() <= 1

@@ -213,6 +213,40 @@ int h3b_dequant_int4_grouped_to_int8(const void* qweight, const void* s_rel, int
                      "dequant_int4_grouped_to_int8");
 }
 
+int h3b_w4a8_group_sums(const void* xq, const void* xs, int64_t M, int64_t K, int64_t G, void* sx,
+                        int64_t sx_row_stride, void* stream) {
+  if (M == 0) return ok();
+  if (!xq || !xs || !sx) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (M < 0 || K <= 0 || G <= 0 || K % G) return fail(H3B_ERR_INVALID_ARGUMENT, "K must be a positive multiple of G");
+  if (sx_row_stride < K / G) return fail(H3B_ERR_INVALID_ARGUMENT, "sx_row_stride < K/G");
+  if (K > INT_MAX || M * sx_row_stride > (int64_t)INT_MAX * 256)
+    return fail(H3B_ERR_UNSUPPORTED, "w4a8_group_sums: sizes too large");
+  return cuda_status(h3b::launch_group_sums(static_cast<const int8_t*>(xq), static_cast<const float*>(xs), M, K, G,
+                                            static_cast<uint16_t*>(sx), sx_row_stride, st(stream)),
+                     "w4a8_group_sums");
+}
+
+int h3b_bf16_gemm_accumulate(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
+                             int64_t out_row_stride, void* stream) {
+  if (M == 0 || N == 0) return ok();
+  if (!A || !B || !D) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (M < 0 || N < 0 || K <= 0 || K % 8 || M > INT_MAX || N > INT_MAX || K > INT_MAX / 2)
+    return fail(H3B_ERR_UNSUPPORTED, "bf16_gemm_accumulate: need K % 8 == 0 and sizes < 2^31");
+  if (out_row_stride < N || out_row_stride % 2) return fail(H3B_ERR_INVALID_ARGUMENT, "bad out_row_stride");
+  if (!aligned16(A) || !aligned16(B) || (reinterpret_cast<uintptr_t>(D) & 3u))
+    return fail(H3B_ERR_UNSUPPORTED, "A, B must be 16-byte and D 4-byte aligned");
+  h3b::GemmArgs g{};
+  g.out = static_cast<uint16_t*>(D);
+  g.out_stride = out_row_stride;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)(2 * K);  // bytes: the kernel walks K in 128-byte steps
+  cudaError_t e = cudaSuccess;
+  const int r = h3b::launch_gemm(A, B, g, h3b::kEpiAddF32, st(stream), &e);
+  if (r == 1) return fail(H3B_ERR_CUDA, "bf16_gemm_accumulate: cuTensorMapEncodeTiled failed");
+  return cuda_status(e, "bf16_gemm_accumulate");
+}
+
 int64_t h3b_key_mean_workspace_bytes(int64_t L, int64_t H) { return h3b::key_mean_workspace(L, H); }
 
 int h3b_key_mean(const void* k, int64_t L, int64_t H, int64_t k_row_stride, void* mean, void* workspace,

@@ -39,6 +39,23 @@ struct GemmSmem {
 __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], int m, int n0, const GemmArgs& a,
                                                 float xs_m, int kind) {
   const int N = a.N;
+  if (kind == kEpiAddF32) {
+    uint16_t* dst = a.out + (int64_t)m * a.out_stride + n0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const int n = n0 + j;
+      if (n + 1 < N) {
+        const uint32_t o = *reinterpret_cast<const uint32_t*>(dst + j);
+        const float y0 = __fadd_rn(__uint_as_float(o << 16), __uint_as_float(r[j]));
+        const float y1 = __fadd_rn(__uint_as_float(o & 0xffff0000u), __uint_as_float(r[j + 1]));
+        *reinterpret_cast<uint32_t*>(dst + j) =
+            (uint32_t)f32_to_bf16_bits(y0) | ((uint32_t)f32_to_bf16_bits(y1) << 16);
+      } else if (n < N) {
+        dst[j] = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(dst[j]), __uint_as_float(r[j])));
+      }
+    }
+    return;
+  }
   if (kind == kEpiInt32) {
     int32_t* dst = a.out_i32 + (int64_t)m * a.out_stride + n0;
     if (n0 + 32 <= N && (a.out_stride % 4) == 0) {
@@ -250,8 +267,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-          tma_load_2d(sa, &tmA, &full[stage], kb * kBK, mb * kBM);
-          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, nb * BN);
+          // the tensor maps count elements: 128 int8 or 64 bf16 per 128-byte K step
+          const int kx = KIND == kEpiAddF32 ? kb * (kBK / 2) : kb * kBK;
+          tma_load_2d(sa, &tmA, &full[stage], kx, mb * kBM);
+          tma_load_2d(sb, &tmB, &full[stage], kx, nb * BN);
         }
         __syncwarp();
         if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -266,7 +285,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // MMA issuer: the whole warp runs the loop (so descriptors stay in uniform
     // registers), one elected lane issues tcgen05.mma / commit
-    constexpr uint32_t idesc = idesc_i8(kBM, BN);
+    constexpr uint32_t idesc = KIND == kEpiAddF32 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN);
     const uint32_t smem_base = smem_u32(smem);
     int stage = 0;
     uint32_t phase = 0;
@@ -285,8 +304,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (elect_one()) {
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
-            // +32 bytes of K per MMA: +2 in the descriptor's 16-byte address units
-            mma_i8_ss(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            // +32 bytes of K per MMA (32 int8 or 16 bf16): +2 in the descriptor's 16-byte units
+            if constexpr (KIND == kEpiAddF32)
+              mma_bf16_ss(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_i8_ss(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
         }
@@ -310,7 +332,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       __syncwarp();
       const int m = mb * kBM + row_in_tile;
-      const float xs_m = (KIND != kEpiInt32 && m < a.M) ? __ldg(a.xs + m) : 0.0f;
+      const float xs_m = (KIND != kEpiInt32 && KIND != kEpiAddF32 && m < a.M) ? __ldg(a.xs + m) : 0.0f;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -687,7 +709,7 @@ bool gemm_uses_pair_kernel(int64_t M, int64_t N) {
 // Returns 0 on success, 1 if a tensor map could not be encoded, 2 on a CUDA error,
 // 4 if the q/k epilogue was asked for a shape that runs the 1-SM kernel.
 int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t s, cudaError_t* err) {
-  if (gemm_uses_pair_kernel(a.M, a.N)) {
+  if (kind != kEpiAddF32 && gemm_uses_pair_kernel(a.M, a.N)) {
     // 2-SM kernel: A rows and B rows in boxes of 128 (each CTA's half of a 256 tile)
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K, kBK,
@@ -706,6 +728,22 @@ int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t
   }
   if (kind == kEpiQkRope64 || kind == kEpiQkRope48) return 4;
   const int tiles256 = ((a.M + kBM - 1) / kBM) * ((a.N + 255) / 256);
+  if (kind == kEpiAddF32) {
+    // bf16 operands [rows, a.K / 2] (a.K counts bytes); 64 elements = 128 bytes per box row
+    const int BNf = (tiles256 >= num_sms() || a.N > 128) ? 256 : 128;
+    const uint64_t kel = (uint64_t)a.K / 2;
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kel, (uint64_t)a.M, (uint64_t)a.K, kBK / 2, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return 1;
+    if (!make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kel, (uint64_t)a.N, (uint64_t)a.K, kBK / 2,
+                      (uint32_t)BNf, CU_TENSOR_MAP_SWIZZLE_128B))
+      return 1;
+    cudaError_t e = BNf == 256 ? launch_gemm_bn<256, kEpiAddF32>(ta, tb, a, s)
+                               : launch_gemm_bn<128, kEpiAddF32>(ta, tb, a, s);
+    *err = e;
+    return e == cudaSuccess ? 0 : 2;
+  }
   const int BN = (tiles256 >= num_sms() || a.N > 128) ? 256 : 128;
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K, kBK, kBM,

@@ -24,7 +24,10 @@ int quant_threads_for(int K);
 
 // kEpiQkRope64 / 48: the store epilogue of the QKV projection with the per-head q/k
 // RMSNorm and split-half RoPE (rotary half-width 64 or 48) applied before the store
-enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiInt32 = 2, kEpiQkRope64 = 3, kEpiQkRope48 = 4 };
+// kEpiAddF32: bf16 x bf16 operands (kind::f16, K in bytes = 2 x elements), the fp32
+// product added into the bf16 output in place: D = bf16(float(D) + acc)
+enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiInt32 = 2, kEpiQkRope64 = 3, kEpiQkRope48 = 4,
+                     kEpiAddF32 = 5 };
 struct GemmArgs {
   int M, N, K;
   const float* xs;
@@ -53,6 +56,10 @@ int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t
 bool make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
                   uint64_t rows, uint64_t stride_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw);
 
+// sx[m, g] = bf16(bf16(sum of xq[m, g*G .. g*G+G-1]) * bf16(xs[m])) for g < K/G, columns
+// [K/G, sx_stride) zero: the W4A8 group-correction activations
+cudaError_t launch_group_sums(const int8_t* xq, const float* xs, int64_t M, int64_t K, int64_t G, uint16_t* sx,
+                              int64_t sx_stride, cudaStream_t s);
 cudaError_t launch_w4_decode(const void* qw, const void* s_rel, int s_rel_kind, const void* codebook, void* out,
                              int64_t N, int64_t K, int64_t G, cudaStream_t s);
 

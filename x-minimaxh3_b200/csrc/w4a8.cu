@@ -67,6 +67,50 @@ __global__ void __launch_bounds__(256) w4_decode_kernel(const uint8_t* __restric
   *reinterpret_cast<uint4*>(dst + 16) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
 }
 
+// ------------------------------------------------------------------ group-correction activations
+// The rank-(K/G) correction of asymmetric W4A8 weights (comfy_kitchen
+// backends/cuda/__init__.py:2294-2297): sx[m, g] = bf16(bf16(sum_{k in group g} xq[m, k])
+// * bf16(xs[m])), the operand of the bf16 GEMM that adds sx @ correction to the output.
+// One thread per (row, group column); columns past the last group are written 0 so
+// the GEMM's K can be padded to a multiple of 8.
+__global__ void __launch_bounds__(256) group_sums_kernel(const int8_t* __restrict__ xq, const float* __restrict__ xs,
+                                                         int64_t M, int K, int G, int groups,
+                                                         uint16_t* __restrict__ sx, int64_t stride) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * stride) return;
+  const int64_t m = i / stride;
+  const int g = (int)(i - m * stride);
+  uint16_t out = 0;
+  if (g < groups) {
+    const int8_t* p = xq + m * (int64_t)K + (int64_t)g * G;
+    int sum = 0;
+    if ((G & 15) == 0 && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+      for (int k = 0; k < G; k += 16) {
+        const int4 w = *reinterpret_cast<const int4*>(p + k);
+        const int ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          sum += (int)(int8_t)(ws[j] & 0xff) + (int)(int8_t)((ws[j] >> 8) & 0xff) +
+                 (int)(int8_t)((ws[j] >> 16) & 0xff) + (int)(int8_t)((ws[j] >> 24) & 0xff);
+      }
+    } else {
+      for (int k = 0; k < G; ++k) sum += p[k];
+    }
+    const float sb = bf16_bits_to_f32(f32_to_bf16_bits((float)sum));   // int32 -> bf16 (exact to float first)
+    const float xb = bf16_bits_to_f32(f32_to_bf16_bits(xs[m]));
+    out = f32_to_bf16_bits(__fmul_rn(sb, xb));
+  }
+  sx[i] = out;
+}
+
+cudaError_t launch_group_sums(const int8_t* xq, const float* xs, int64_t M, int64_t K, int64_t G, uint16_t* sx,
+                              int64_t sx_stride, cudaStream_t s) {
+  const int64_t total = M * sx_stride;
+  group_sums_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(xq, xs, M, (int)K, (int)G, (int)(K / G), sx,
+                                                                    sx_stride);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_w4_decode(const void* qw, const void* s_rel, int s_rel_kind, const void* codebook, void* out,
                              int64_t N, int64_t K, int64_t G, cudaStream_t s) {
   const int64_t total = N * (K / 32);

@@ -60,6 +60,8 @@ _SIGNATURES = {
     "h3b_int8_gemm_i32": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p],
     "h3b_dequant_int4_grouped_to_int8": [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                          c_void_p],
+    "h3b_w4a8_group_sums": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p],
+    "h3b_bf16_gemm_accumulate": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
     "h3b_key_mean_workspace_bytes": [c_int64, c_int64],
     "h3b_key_mean": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
     "h3b_key_mean_no_alloc": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],

@@ -360,14 +360,38 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     return out.reshape(*x.shape[:-1], N)
 
 
+def correction_operand(correction: torch.Tensor) -> torch.Tensor:
+    """correction [K/G, N] -> the bf16 B operand [N, pad8(K/G)] of the correction GEMM
+    (transposed so each output column's groups are contiguous; zero columns pad K to 8).
+    A weight: build it once per layer."""
+    groups, N = correction.shape
+    kp = (groups + 7) // 8 * 8
+    op = torch.zeros((N, kp), device=correction.device, dtype=torch.bfloat16)
+    op[:, :groups] = correction.to(torch.bfloat16).t()
+    return op
+
+
 def w4a8_group_correction_(out: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, correction: torch.Tensor,
-                           group_size: int) -> torch.Tensor:
-    """out += (sum of each group's activation codes * xs) @ correction [K/G, N], in out's dtype."""
+                           group_size: int, operand: torch.Tensor | None = None) -> torch.Tensor:
+    """out += (sum of each group's activation codes * xs) @ correction [K/G, N], in bf16 with
+    fp32 accumulation (comfy_kitchen backends/cuda/__init__.py:2294-2297): the group sums
+    (h3b_w4a8_group_sums) then a tcgen05 bf16 GEMM accumulating into out
+    (h3b_bf16_gemm_accumulate).  `operand`: correction_operand(correction), if cached."""
+    _cuda("w4a8_group_correction_", out, xq, xs, correction)
     M, K = xq.shape
     groups = K // group_size
     N = out.shape[-1]
     if tuple(correction.shape) != (groups, N):
         raise ValueError(f"correction must have shape {(groups, N)}, got {tuple(correction.shape)}")
-    # (sum of each group's codes) * xs @ correction, as the reference CUDA path
-    sx = xq.view(M, groups, group_size).sum(-1, dtype=torch.int32).to(out.dtype) * xs.reshape(M, 1).to(out.dtype)
-    return out.addmm_(sx, correction.to(out.dtype))
+    if out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("the W4A8 correction accumulates into bfloat16 rows")
+    op = correction_operand(correction) if operand is None else operand
+    kp = op.shape[1]
+    sx = torch.empty((M, kp), device=xq.device, dtype=torch.bfloat16)
+    xs2 = xs.reshape(-1).to(torch.float32).contiguous()
+    check(lib().h3b_w4a8_group_sums(_p(xq.contiguous()), _p(xs2), M, K, group_size, _p(sx), kp, _stream(xq)),
+          "w4a8_group_sums")
+    out2 = out.view(-1, N) if out.is_contiguous() else out
+    check(lib().h3b_bf16_gemm_accumulate(_p(sx), _p(op), _p(out2), M, N, kp, out2.stride(0), _stream(xq)),
+          "bf16_gemm_accumulate")
+    return out

@@ -277,7 +277,10 @@ class W4A8Linear(_QuantLinear):
 
     def _correct_(self, out, xq, xs) -> None:
         if self.correction is not None:
-            ops.w4a8_group_correction_(out, xq, xs, self.correction, self.spec.group_size)
+            if getattr(self, "_correction_operand", None) is None:
+                self._correction_operand = ops.correction_operand(self.correction)
+            ops.w4a8_group_correction_(out, xq, xs, self.correction, self.spec.group_size,
+                                       self._correction_operand)
 
     def dense_weight(self) -> torch.Tensor:
         """fp32 [N, K] weight (model/quantization.py:486-516 decode order)."""
