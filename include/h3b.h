@@ -40,6 +40,7 @@ extern "C" {
 /* device status codes (h3b_device_status) */
 #define H3B_STATUS_GEMM_TIMEOUT -101
 #define H3B_STATUS_ATTN_TIMEOUT -102
+#define H3B_STATUS_SELFTEST_TIMEOUT -103
 
 /* ---------------------------------------------------------------- library */
 
@@ -53,6 +54,14 @@ const char* h3b_last_error(void);
  * problem) into *status; clears it when `reset` is non-zero.  Synchronizes
  * the device. */
 int h3b_device_status(int device, int* status, int reset);
+
+/* Exercises the kernels' bounded-wait failure path on purpose: one warp waits on a
+ * hardware barrier that nothing will release, with the same wait routine the GEMM and
+ * attention kernels use but a limit of `limit_ns` (at most 1 s); it gives up, records
+ * H3B_STATUS_SELFTEST_TIMEOUT in the device status word and returns.  The CUDA context
+ * stays usable.  For tests of the failure handling; no counterpart in the reference
+ * (whose kernels do not bound their waits). */
+int h3b_selftest_bounded_wait(int64_t limit_ns, void* stream);
 
 /* ---------------------------------------------------------------- quantization */
 

@@ -59,6 +59,9 @@ def test_unsupported_shapes_are_rejected():
     assert lib().h3b_attention(dummy, ctypes.c_void_p(20), 0, 128, 10, 128, dummy, ctypes.c_void_p(20), 1, 10, 128,
                                dummy, dummy, 1, None, 0.1, dummy, 128, None) == -2
     assert lib().h3b_quantize_per_thread_int8(dummy, 10, 1, 128, None, 2, dummy, dummy, 128, None) == -1
+    assert lib().h3b_selftest_bounded_wait(0, None) == -1
+    assert lib().h3b_selftest_bounded_wait(2_000_000_000, None) == -1
+    assert lib().h3b_bf16_gemm_accumulate(dummy, dummy, dummy, 8, 8, 12, 8, None) == -2
 
 
 def test_qkv_qk_rope_entry_rejects_what_it_does_not_take():

@@ -90,20 +90,41 @@ static __device__ __align__(256) double g_key_mean_scratch[kKeyMeanScratchDouble
 
 // Device address of g_key_mean_scratch, looked up once per device with that
 // device current (in host code the array's name is only a host-side stand-in).
+// The lookup is remembered together with the CUDA context it was made in: after a
+// cudaDeviceReset, or under another context on the same device, the module may sit
+// at another address, so a changed context means a fresh lookup.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 static std::mutex g_scratch_mu;
 static double* g_scratch_ptr[64] = {};
+static CUcontext g_scratch_ctx[64] = {};
+
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  CUcontext c = nullptr;
+  if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
 
 static cudaError_t key_mean_scratch_for_current_device(double** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const CUcontext ctx = current_context();  // null until a runtime call made one current
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  if (!g_scratch_ptr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_key_mean_scratch);
+    e = cudaGetSymbolAddress(&p, g_key_mean_scratch);  // makes the device's context current
     if (e != cudaSuccess) return e;
     g_scratch_ptr[dev] = static_cast<double*>(p);
+    g_scratch_ctx[dev] = current_context();
   }
   *out = g_scratch_ptr[dev];
   return cudaSuccess;

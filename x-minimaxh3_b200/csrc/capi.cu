@@ -27,6 +27,22 @@ int cuda_status(cudaError_t e, const char* what) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 cudaStream_t st(void* s) { return static_cast<cudaStream_t>(s); }
 
+// The bounded-wait failure path of the kernels, exercised on purpose: one warp
+// waits on an mbarrier that nothing arrives at, with the kernels' own wait routine
+// and a short limit; it gives up, records `code` in the device status word and
+// returns, leaving the context usable.
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns, int code) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    h3b::mbar_init(&bar, 1);
+    abort_flag = 0;
+    h3b::fence_mbar_init();
+  }
+  __syncthreads();
+  h3b::mbar_wait_for(&bar, 0, &abort_flag, code, limit_ns);
+}
+
 }  // namespace
 
 extern "C" {
@@ -49,6 +65,13 @@ int h3b_device_status(int device, int* status, int reset) {
   }
   cudaSetDevice(prev);
   return cuda_status(e, "h3b_device_status");
+}
+
+int h3b_selftest_bounded_wait(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 1000000000LL)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 1 s]");
+  bounded_wait_selftest_kernel<<<1, 32, 0, st(stream)>>>((uint64_t)limit_ns, H3B_STATUS_SELFTEST_TIMEOUT);
+  return cuda_status(cudaGetLastError(), "selftest_bounded_wait");
 }
 
 int h3b_quantize_int8_rowwise(const void* x, int64_t rows, int64_t cols, int64_t x_row_stride, void* q, void* scales,

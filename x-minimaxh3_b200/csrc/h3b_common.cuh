@@ -146,19 +146,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // and a try count, so the wait ends even if the timer were not to advance.
 // Returns false on timeout or abort.
 constexpr uint32_t kWaitMaxTries = 1u << 26;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int code) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t n = 0;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (n >= kWaitMaxTries || globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (n >= kWaitMaxTries || globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       record_status(code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int code) {
+  return mbar_wait_for(bar, parity, abort_flag, code, kWaitLimitNs);
 }
 // Warp-wide bounded wait: every lane waits, then the warp agrees on the outcome,
 // so warp-collective (.sync.aligned) instructions after it run converged.

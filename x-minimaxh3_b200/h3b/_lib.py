@@ -45,6 +45,7 @@ _SIGNATURES = {
     "h3b_version": [],
     "h3b_last_error": [],
     "h3b_device_status": [c_int, ctypes.POINTER(c_int), c_int],
+    "h3b_selftest_bounded_wait": [c_int64, c_void_p],
     "h3b_quantize_int8_rowwise": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "h3b_quantize_int8_rowwise_convrot": [c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p,
                                           c_void_p],
