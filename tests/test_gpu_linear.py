@@ -313,6 +313,6 @@ def test_w4a8_group_correction_native(ops, m, k, g, n):
     assert ulps.max() <= 1 and (ulps == 0).mean() >= 0.99, (ulps.max(), (ulps == 0).mean())
     # the reference's eager formula, on the GPU (cuBLAS)
     sx = xq.cuda().view(m, k // g, g).sum(-1, dtype=torch.int32).to(torch.bfloat16)
-    sx = sx * xs.cuda().to(torch.bfloat16)
+    sx = sx * xs.cuda().reshape(m, 1).to(torch.bfloat16)
     ref = out0.cuda().addmm_(sx, corr.cuda())
     assert _bf16_ulps(bits(out), bits(ref)).max() <= 1
