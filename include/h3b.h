@@ -302,6 +302,23 @@ int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, cons
  * Replaces parallel_block_map_lut (model/sparse_lut.py:144-192). */
 int h3b_bitmap_to_lut(const void* bitmap, int64_t rows, int64_t Kb, void* lut, void* valid, void* stream);
 
+/* ---------------------------------------------------------------- Ulysses layouts */
+
+/* The send buffer of the token -> head all-to-all over P ranks, from this rank's rows:
+ * dst[p][l][j][:] = src[l][head_order[p*H/P + j]][:] (head_order NULL: head p*H/P + j),
+ * 128 bf16 channels per head.  src: bf16 rows [rows, src_row_stride] whose first H*128
+ * columns are the heads (e.g. the K slot of the QKV projection rows); dst: bf16
+ * [P, rows, H/P, 128].  head_order: device int64 [H], a permutation.  No counterpart in
+ * the reference (single-GPU); replaces a gather and a transposed copy in torch. */
+int h3b_ulysses_pack(const void* src, int64_t rows, int64_t H, int64_t src_row_stride, const int64_t* head_order,
+                     int64_t P, void* dst, void* stream);
+
+/* The inverse for the head -> token all-to-all's result: dst[l][head_order[p*H/P + j]][:]
+ * = src[p][l][j][:], writing token rows [rows, dst_row_stride] in head index order.
+ * src: bf16 [P, rows, H/P, 128]. */
+int h3b_ulysses_unpack(const void* src, int64_t rows, int64_t H, const int64_t* head_order, int64_t P, void* dst,
+                       int64_t dst_row_stride, void* stream);
+
 /* ---------------------------------------------------------------- attention */
 
 /* O = softmax(Q K^T * sm_scale) V with INT8 Q.K^T (tcgen05 kind::i8), fp32

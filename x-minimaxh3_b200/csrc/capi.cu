@@ -384,6 +384,34 @@ int h3b_value_fp8_given_absmax(const void* v, int64_t rows, int64_t H, int64_t v
                      "value_fp8_given_absmax");
 }
 
+static int check_heads_args(int64_t rows, int64_t H, int64_t P, const void* a, const void* b) {
+  if (!a || !b) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (rows < 0 || H <= 0 || P <= 0 || H % P) return fail(H3B_ERR_INVALID_ARGUMENT, "H must be a multiple of P");
+  if (!aligned16(a) || !aligned16(b)) return fail(H3B_ERR_UNSUPPORTED, "buffers must be 16-byte aligned");
+  if (rows * H * 16 > (int64_t)INT_MAX * 256) return fail(H3B_ERR_UNSUPPORTED, "too many rows");
+  return H3B_OK;
+}
+
+int h3b_ulysses_pack(const void* src, int64_t rows, int64_t H, int64_t src_row_stride, const int64_t* head_order,
+                     int64_t P, void* dst, void* stream) {
+  if (rows == 0) return ok();
+  const int r = check_heads_args(rows, H, P, src, dst);
+  if (r != H3B_OK) return r;
+  if (src_row_stride < H * 128 || src_row_stride % 8) return fail(H3B_ERR_INVALID_ARGUMENT, "bad src_row_stride");
+  return cuda_status(h3b::launch_gather_heads(src, rows, H, src_row_stride, head_order, P, dst, st(stream)),
+                     "ulysses_pack");
+}
+
+int h3b_ulysses_unpack(const void* src, int64_t rows, int64_t H, const int64_t* head_order, int64_t P, void* dst,
+                       int64_t dst_row_stride, void* stream) {
+  if (rows == 0) return ok();
+  const int r = check_heads_args(rows, H, P, src, dst);
+  if (r != H3B_OK) return r;
+  if (dst_row_stride < H * 128 || dst_row_stride % 8) return fail(H3B_ERR_INVALID_ARGUMENT, "bad dst_row_stride");
+  return cuda_status(h3b::launch_scatter_heads(src, rows, H, head_order, P, dst, dst_row_stride, st(stream)),
+                     "ulysses_unpack");
+}
+
 int h3b_block_mask(const void* pooled_q, const void* similar_q, int64_t Qb, const void* pooled_k,
                    const void* similar_k, int64_t Kb, int64_t H, const h3b_mask_params* p, void* bitmap,
                    void* stream) {

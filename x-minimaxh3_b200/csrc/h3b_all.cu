@@ -6,4 +6,5 @@
 #include "attn_prep.cu"
 #include "attn_mask.cu"
 #include "attn.cu"
+#include "ulysses.cu"
 #include "capi.cu"

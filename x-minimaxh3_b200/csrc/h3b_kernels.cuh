@@ -140,4 +140,10 @@ struct AttnArgs {
 int launch_attention(const void* q, const void* k, const void* vt, const AttnArgs& a, cudaStream_t s,
                      cudaError_t* err);
 
+// Ulysses all-to-all layouts (ulysses.cu): bf16 heads of 128 channels
+cudaError_t launch_gather_heads(const void* src, int64_t rows, int64_t H, int64_t src_stride, const int64_t* order,
+                                int64_t P, void* dst, cudaStream_t s);
+cudaError_t launch_scatter_heads(const void* src, int64_t rows, int64_t H, const int64_t* order, int64_t P,
+                                 void* dst, int64_t dst_stride, cudaStream_t s);
+
 }  // namespace h3b

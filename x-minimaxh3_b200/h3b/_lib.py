@@ -77,6 +77,8 @@ _SIGNATURES = {
     "h3b_qk_rmsnorm_rope": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_int, c_float, c_void_p],
     "h3b_value_fp8": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "h3b_ulysses_pack": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    "h3b_ulysses_unpack": [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p],
     "h3b_block_mask": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                        ctypes.POINTER(MaskParams), c_void_p, c_void_p],
     "h3b_bitmap_to_lut": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],

@@ -47,6 +47,50 @@ def tokens_to_heads(qkv: torch.Tensor, heads: int, head_dim: int, group=None) ->
     return recv.view(P * Lp, 3 * hd)
 
 
+def _pack(src: torch.Tensor, rows: int, heads: int, head_dim: int, P: int, order: torch.Tensor | None) -> torch.Tensor:
+    """[rows, heads, D] view (unit stride in the last two dims) -> send buffer [P, rows, H/P * D].
+    CUDA tensors take the native kernel (h3b_ulysses_pack: one read, one write); CPU
+    tensors (gloo process groups, the host-side tests of the exchange) take the same
+    layout in torch."""
+    hpr = heads // P
+    if not src.is_cuda:
+        if order is not None:
+            src = src.index_select(1, order)
+        return src.reshape(rows, P, hpr * head_dim).permute(1, 0, 2).contiguous()
+    from ._lib import check, lib
+    from .ops import _p, _stream
+
+    if head_dim != 128 or src.dtype != torch.bfloat16 or src.stride(2) != 1 or src.stride(1) != 128:
+        raise ValueError("the Ulysses pack kernel takes bf16 heads of 128 contiguous channels")
+    dst = torch.empty((P, rows, hpr * head_dim), device=src.device, dtype=src.dtype)
+    o = None if order is None else order.to(device=src.device, dtype=torch.int64).contiguous()
+    check(lib().h3b_ulysses_pack(_p(src), rows, heads, src.stride(0), _p(o), P, _p(dst), _stream(src)),
+          "ulysses_pack")
+    return dst
+
+
+def _unpack(recv: torch.Tensor, rows: int, P: int, hd: int, order: torch.Tensor | None) -> torch.Tensor:
+    """[P, rows, hd] received chunks -> token rows [rows, P*hd] in head index order."""
+    if not recv.is_cuda:
+        tokens = recv.view(P, rows, hd).permute(1, 0, 2).reshape(rows, P * hd)
+        if order is None:
+            return tokens
+        heads = order.numel()
+        D = P * hd // heads
+        out = torch.empty_like(tokens)
+        out.view(rows, heads, D).index_copy_(1, order, tokens.view(rows, heads, D))
+        return out
+    from ._lib import check, lib
+    from .ops import _p, _stream
+
+    heads = P * hd // 128
+    out = torch.empty((rows, P * hd), device=recv.device, dtype=recv.dtype)
+    o = None if order is None else order.to(device=recv.device, dtype=torch.int64).contiguous()
+    check(lib().h3b_ulysses_unpack(_p(recv), rows, heads, _p(o), P, _p(out), out.stride(0), _stream(recv)),
+          "ulysses_unpack")
+    return out
+
+
 def exchange_qkv_async(qkv: torch.Tensor, heads: int, head_dim: int, group=None,
                        order: torch.Tensor | None = None) -> dict[str, tuple[torch.Tensor, object]]:
     """Start the token -> head exchange of K, V and Q (in that order) from the QKV
@@ -63,10 +107,7 @@ def exchange_qkv_async(qkv: torch.Tensor, heads: int, head_dim: int, group=None,
     view = qkv.view(Lp, 3, heads, head_dim)
     out = {}
     for name, slot in (("k", 1), ("v", 2), ("q", 0)):
-        src = view[:, slot]
-        if order is not None:
-            src = src.index_select(1, order)
-        send = src.reshape(Lp, P, hpr * head_dim).permute(1, 0, 2).contiguous()   # [P, Lp, hd]
+        send = _pack(view[:, slot], Lp, heads, head_dim, P, order)   # [P, Lp, hd]
         recv = torch.empty((P * Lp, hpr, head_dim), device=qkv.device, dtype=qkv.dtype)
         work = dist.all_to_all_single(recv.view(P, Lp, hpr * head_dim), send, group=group, async_op=True)
         out[name] = (recv, work)
@@ -80,15 +121,7 @@ def heads_to_tokens(o: torch.Tensor, local_rows: int, group=None, order: torch.T
     send = o.contiguous()
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)
-    hd = o.shape[1]
-    tokens = recv.view(P, local_rows, hd).permute(1, 0, 2).reshape(local_rows, P * hd)
-    if order is None:
-        return tokens
-    heads = order.numel()
-    D = P * hd // heads
-    out = torch.empty_like(tokens)
-    out.view(local_rows, heads, D).index_copy_(1, order, tokens.view(local_rows, heads, D))
-    return out
+    return _unpack(recv, local_rows, P, o.shape[1], order)
 
 
 def balanced_head_order(kept: torch.Tensor, world: int) -> torch.Tensor:
