@@ -314,5 +314,8 @@ def test_w4a8_group_correction_native(ops, m, k, g, n):
     # the reference's eager formula, on the GPU (cuBLAS)
     sx = xq.cuda().view(m, k // g, g).sum(-1, dtype=torch.int32).to(torch.bfloat16)
     sx = sx * xs.cuda().reshape(m, 1).to(torch.bfloat16)
-    ref = out0.cuda().addmm_(sx, corr.cuda())
-    assert _bf16_ulps(bits(out), bits(ref)).max() <= 1
+    ref = out0.cuda().addmm_(sx, corr.cuda()).float().cpu()
+    got = out.float().cpu()
+    # one bf16 rounding apart, or a few 1e-4 where out0 and the correction cancel
+    assert bool(((got - ref).abs() <= torch.maximum(ref.abs() * 2.0 ** -7, torch.tensor(2e-4))).all())
+    assert rel_l2(got, ref) <= 2e-3
