@@ -299,8 +299,9 @@ def _bf16_ulps(a: np.ndarray, b: np.ndarray) -> np.ndarray:
 def test_w4a8_group_correction_native(ops, m, k, g, n):
     """The W4A8 group correction (comfy_kitchen backends/cuda/__init__.py:2294-2297) as two
     native kernels (group sums, then a tcgen05 bf16 GEMM accumulating into the output):
-    within one bf16 ulp of the oracle (which sums the exact bf16 products in double) on
-    every element, and of the reference's own formula (torch addmm on the GPU)."""
+    bit-equal to the oracle (which sums the exact bf16 products in double) on at least 99 %
+    of the elements, every element inside the rounding bound of an fp32 accumulation, and
+    close to the reference's own formula (torch addmm on the GPU)."""
     gen = torch.Generator().manual_seed(m + k + n)
     xq = torch.randint(-127, 128, (m, k), generator=gen, dtype=torch.int16).to(torch.int8)
     xs = torch.rand(m, generator=gen) * 1e-2 + 1e-4
@@ -310,7 +311,17 @@ def test_w4a8_group_correction_native(ops, m, k, g, n):
     ops.w4a8_group_correction_(out, xq.cuda(), xs.cuda(), corr.cuda(), g)
     exp = O.w4a8_correction(xq.numpy(), xs.numpy(), g, bits(corr), bits(out0))
     ulps = _bf16_ulps(bits(out), exp)
-    assert ulps.max() <= 1 and (ulps == 0).mean() >= 0.99, (ulps.max(), (ulps == 0).mean())
+    assert (ulps == 0).mean() >= 0.99, (ulps.max(), (ulps == 0).mean())
+    # every element within the error bound of an fp32-accumulated sum of the exact products
+    # (groups terms; near cancellation a few bf16 ulps of a small result are that bound)
+    sx64 = (xq.view(m, k // g, g).sum(-1, dtype=torch.int32).to(torch.bfloat16)
+            * xs.reshape(m, 1).to(torch.bfloat16)).double()
+    corr64 = corr.double()
+    exact = out0.double() + sx64 @ corr64
+    got64 = out.double().cpu()
+    ulp = torch.ldexp(torch.ones_like(exact), torch.frexp(exact.abs().float())[1].double().long() - 8)
+    bound = ulp + (k // g) * 2.0 ** -23 * (sx64.abs() @ corr64.abs())
+    assert bool(((got64 - exact).abs() <= bound).all()), float(((got64 - exact).abs() / bound).max())
     # the reference's eager formula, on the GPU (cuBLAS)
     sx = xq.cuda().view(m, k // g, g).sum(-1, dtype=torch.int32).to(torch.bfloat16)
     sx = sx * xs.cuda().reshape(m, 1).to(torch.bfloat16)
