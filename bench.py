@@ -133,6 +133,8 @@ KERNEL_CASES = """
     keys                       K mean + pool / similarity / INT8 (prepare_keys), L = 65,536, 32 heads
     values                     V absmax + FP8 transpose (prepare_values), L = 65,536, 32 heads
     w4_decode                  h3b_dequant_int4_grouped_to_int8, 16,384 x 4,096, G = 128
+    gemm_gelu                  h3b_int8_gemm_gelu_convrot (GELU + ConvRot epilogue), 16,384 x 16,384 x 4,096
+    quant_rotated              h3b_quantize_rotated_int8 on its output, 16,384 x 16,384
 """
 
 
@@ -196,6 +198,26 @@ def _kernel_case(name: str, g):
         qd = torch.randint(-128, 128, (N, K // 2), dtype=torch.int8, device=dev, generator=g)
         srel = torch.rand(N, K // G, device=dev, generator=g) * 20 + 1
         return lambda: ops.dequant_int4_grouped_to_int8(qd, srel, None, G)
+    if name in ("gemm_gelu", "quant_rotated"):
+        M, N, K = 16384, 16384, 4096
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        xs = torch.rand(M, device=dev, generator=g) * 1e-2
+        ws = torch.rand(N, device=dev, generator=g) * 1e-2
+        bias = torch.randn(N, device=dev, generator=g)
+        rot = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        amax = torch.empty(M, N // 128, device=dev, dtype=torch.float32)
+        from h3b._lib import check, lib
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def fused():
+            check(lib().h3b_int8_gemm_gelu_convrot(a.data_ptr(), b.data_ptr(), xs.data_ptr(), ws.data_ptr(), N,
+                                                   bias.data_ptr(), rot.data_ptr(), M, N, K, N, amax.data_ptr(),
+                                                   N // 128, stream), "gemm_gelu")
+        if name == "gemm_gelu":
+            return fused
+        fused()
+        return lambda: ops.quantize_rotated_int8(rot, amax)
     raise SystemExit(f"unknown case {name!r}; cases:{KERNEL_CASES}")
 
 
@@ -318,6 +340,24 @@ def run_kernel_table(args, L) -> int:
     row("tanh-GELU + ConvRot INT8 quantizer (K 16384)", ms, L * F * 3 + L * 4, "hbm")
     hq, hs = blk.fc2.quantize(h, cfg.mlp_act)
     del h
+    ms = _timed(lambda: blk.fc1.forward_prequantized_for(blk.fc2, xq2, xs2, cfg.mlp_act), reps)
+    row("FC1 W4A8 with tanh-GELU + ConvRot epilogue, then codes (the block's path)", ms, 2.0 * L * F * D, "tensor")
+    w8, ws8 = blk.fc1.int8_weight()
+    rot = torch.empty(L, F, device="cuda", dtype=torch.bfloat16)
+    amax = torch.empty(L, F // 128, device="cuda", dtype=torch.float32)
+    b32 = blk.fc1.bias.float()
+    from h3b._lib import lib as _lib
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def fused_gemm():
+        _lib().h3b_int8_gemm_gelu_convrot(xq2.data_ptr(), w8.data_ptr(), xs2.data_ptr(), ws8.data_ptr(),
+                                          ws8.numel(), b32.data_ptr(), rot.data_ptr(), L, F, D, F,
+                                          amax.data_ptr(), F // 128, stream)
+    ms = _timed(fused_gemm, reps)
+    row("  of which: INT8 GEMM + GELU + ConvRot epilogue (N 16384, K 4096)", ms, 2.0 * L * F * D, "tensor")
+    ms = _timed(lambda: ops.quantize_rotated_int8(rot, amax), reps)
+    row("  of which: rotated rows -> INT8 codes (K 16384)", ms, L * F * 3 + L * F // 128 * 4 + L * 4, "hbm")
+    del rot, amax
     ms = _timed(lambda: blk.fc2.gated_residual_(xr, gm[0], hq, hs), reps)
     row("FC2 W4A8 + gated residual (N 4096, K 16384)", ms, 2.0 * L * D * F, "tensor")
     step = _timed(lambda: blk.forward(x.clone(), t, rope), 3)

@@ -129,6 +129,33 @@ int h3b_int8_gemm_dequant_qk_rope(const void* A, const void* B, const void* xs, 
                                   const void* q_weight, const void* k_weight, const void* cos_table,
                                   const void* sin_table, int rot_dim, float eps, void* stream);
 
+/* FC1 of the GELU MLP with the first half of FC2's input quantizer in its
+ * epilogue: the bf16 values h3b_int8_gemm_dequant would store go through tanh-GELU
+ * and the ConvRot-256 rotation (every 256-column group), and are stored as bf16
+ * rotated values in D; amax[m * amax_row_stride + 2 t + h] receives the fp32 absmax
+ * of row m's rotated values in columns 256 t + 64 j + 32 h + [0, 32), j = 0..3 (256-column
+ * tile t, half h; N / 128 entries per row, their max is the row's absmax).  Then
+ * h3b_quantize_rotated_int8 forms the codes and row scales, bit-identical to
+ * h3b_int8_gemm_dequant followed by h3b_quantize_int8_rowwise_convrot(input_act = 1).
+ * Returns H3B_ERR_UNSUPPORTED with nothing launched unless the shape runs the 2-SM
+ * kernel (ceil(M/256) * ceil(N/256) >= the SM count), N % 256 == 0, N <= 16384, D is
+ * 16-byte aligned with out_row_stride % 8 == 0 and amax_row_stride >= N / 128; the
+ * caller then makes those two calls.  Replaces the FC1 projection followed by the
+ * FC2 input quantizer with input_act gelu_tanh (model/fused_mlp.py:269-426 feeding
+ * comfy_kitchen int8_linear.cu:943-1030). */
+int h3b_int8_gemm_gelu_convrot(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,
+                               const void* bias, void* D, int64_t M, int64_t N, int64_t K, int64_t out_row_stride,
+                               void* amax, int64_t amax_row_stride, void* stream);
+
+/* Codes and row scales from rotated bf16 rows (the output of
+ * h3b_int8_gemm_gelu_convrot): scale[r] = max(min(absmax, bf16 max) / 127, 1e-30)
+ * with absmax the max of amax[r * amax_row_stride + c], c < amax_cols, and
+ * q[r, k] = clamp(rint(bf16(rot[r, k] / bf16(scale[r]))), -128, 127).
+ * rot: bf16 [rows, rot_row_stride]; q: int8 [rows, cols]; scales: f32 [rows].
+ * cols % 8 == 0, cols <= 16384, rot and q 16-byte aligned, rot_row_stride % 8 == 0. */
+int h3b_quantize_rotated_int8(const void* rot, int64_t rows, int64_t cols, int64_t rot_row_stride, const void* amax,
+                              int64_t amax_row_stride, int64_t amax_cols, void* q, void* scales, void* stream);
+
 /* As h3b_int8_gemm_dequant, but the bf16 result y[m,n] is added into a bf16
  * residual stream in place: residual[m,n] = bf16(residual + y * gate[n])
  * (gate: bf16 [N]).  Replaces int8_linear followed by residual.addcmul_

@@ -327,6 +327,8 @@ def test_w4a8_group_correction_native(ops, m, k, g, n):
     sx = sx * xs.cuda().reshape(m, 1).to(torch.bfloat16)
     ref = out0.cuda().addmm_(sx, corr.cuda()).float().cpu()
     got = out.float().cpu()
-    # one bf16 rounding apart, or a few 1e-4 where out0 and the correction cancel
-    assert bool(((got - ref).abs() <= torch.maximum(ref.abs() * 2.0 ** -7, torch.tensor(2e-4))).all())
-    assert rel_l2(got, ref) <= 2e-3
+    # cuBLAS may round the product before the add: one bf16 ulp of the larger of the
+    # result and the correction term (the term can cancel against out0)
+    term = (sx.float() @ corr.cuda().float()).abs().cpu()
+    assert bool(((got - ref).abs() <= (ref.abs() + term) * 2.0 ** -7 + 2e-4).all())
+    assert rel_l2(got, ref) <= 4e-3   # two bf16 roundings apart at most

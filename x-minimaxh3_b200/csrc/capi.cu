@@ -198,6 +198,47 @@ int h3b_int8_gemm_dequant_qk_rope(const void* A, const void* B, const void* xs, 
                      "int8_gemm_dequant_qk_rope");
 }
 
+int h3b_int8_gemm_gelu_convrot(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,
+                               const void* bias, void* D, int64_t M, int64_t N, int64_t K, int64_t out_row_stride,
+                               void* amax, int64_t amax_row_stride, void* stream) {
+  if (!xs || !ws || !D || !amax) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ws_numel != 1 && ws_numel != N) return fail(H3B_ERR_INVALID_ARGUMENT, "ws_numel must be 1 or N");
+  if (out_row_stride < N || amax_row_stride < N / 128)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "out_row_stride < N or amax_row_stride < N / 128");
+  if (N % 256 || N > 16384)
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: need N % 256 == 0 and N <= 16384");
+  if (!aligned16(D) || out_row_stride % 8)
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: D must be 16-byte aligned, out_row_stride % 8 == 0");
+  if (M > 0 && N > 0 && !h3b::gemm_uses_pair_kernel(M, N))
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: the shape does not run the 2-SM kernel");
+  h3b::GemmArgs g{};
+  g.xs = static_cast<const float*>(xs);
+  g.ws = static_cast<const float*>(ws);
+  g.ws_scalar = ws_numel == 1;
+  g.bias = static_cast<const float*>(bias);
+  g.out = static_cast<uint16_t*>(D);
+  g.out_stride = out_row_stride;
+  g.amax = static_cast<float*>(amax);
+  g.amax_stride = amax_row_stride;
+  return gemm_common(A, B, M, N, K, g, h3b::kEpiGeluRot, stream, "int8_gemm_gelu_convrot");
+}
+
+int h3b_quantize_rotated_int8(const void* rot, int64_t rows, int64_t cols, int64_t rot_row_stride, const void* amax,
+                              int64_t amax_row_stride, int64_t amax_cols, void* q, void* scales, void* stream) {
+  if (rows == 0 || cols == 0) return ok();
+  if (!rot || !amax || !q || !scales) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (rows < 0 || cols < 0 || amax_cols <= 0 || amax_row_stride < amax_cols || rot_row_stride < cols)
+    return fail(H3B_ERR_INVALID_ARGUMENT, "quantize_rotated_int8: bad sizes or strides");
+  if (cols % 8 || cols > 16384 || rot_row_stride % 8 || amax_cols > INT_MAX)
+    return fail(H3B_ERR_UNSUPPORTED, "quantize_rotated_int8: need cols % 8 == 0, cols <= 16384, stride % 8 == 0");
+  if (!aligned16(rot) || !aligned16(q)) return fail(H3B_ERR_UNSUPPORTED, "rot and q must be 16-byte aligned");
+  return cuda_status(h3b::launch_quant_rotated(static_cast<const uint16_t*>(rot), rot_row_stride,
+                                               static_cast<const float*>(amax), amax_row_stride, (int)amax_cols,
+                                               (int)cols, rows, static_cast<int8_t*>(q), static_cast<float*>(scales),
+                                               st(stream)),
+                     "quantize_rotated_int8");
+}
+
 int h3b_int8_gemm_gated_residual(const void* A, const void* B, const void* xs, const void* ws, int64_t ws_numel,
                                  const void* bias, const void* gate, void* residual, int64_t M, int64_t N, int64_t K,
                                  int64_t residual_row_stride, void* stream) {

@@ -15,6 +15,7 @@
 // Tiles are walked M-major (all N tiles of one 128-row band before the next
 // band) so the A band and the whole weight matrix stay L2-resident.
 #include "h3b_kernels.cuh"
+#include "h3b_packed.cuh"
 
 namespace h3b {
 
@@ -222,6 +223,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;        // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // GELU + ConvRot exchange: [quadrant][half][accumulator], "this half's values are in TMEM"
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (a.M + kBM - 1) / kBM, num_n = (a.N + BN - 1) / BN;
@@ -382,8 +385,126 @@ struct PairSmem {
   static constexpr int kBBytes = (PBN / 2) * kBK;  // this CTA's half of the B tile
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = kStages * kStageBytes;
-  static constexpr int kTotal = kBarOffset + 256 + 1024;
+  static constexpr int kTotal = kBarOffset + 512 + 1024;  // barriers + alignment slack
 };
+
+// ---------------------------------------------------------------- GELU + ConvRot epilogue
+// A 256-column tile of FC1 holds one ConvRot group of each of its rows.  The two
+// epilogue warps of a TMEM lane quadrant split it: warp hh takes 64-column blocks
+// 2hh and 2hh + 1 as the two lanes of packed pairs.  Each value is the store
+// epilogue's bf16 output (dequantized, bias added, rounded), then tanh-GELU, then
+// the stride-1, -4 and -16 radix-4 stages of the transform, which stay inside a
+// 64-column block; the results go back into the warp's own accumulator columns.
+// After the partner warp has done the same, warp hh runs the stride-64 stage for
+// butterfly positions [32 hh, 32 hh + 32) of the four blocks, stores the rotated
+// values as bf16 and the absmax of its 128 fp32 outputs.  Every value passes the
+// same butterflies with the same operands as in the standalone quantizer
+// (quant_rows_kernel<kConvRot, gelu>), so the codes formed from these values equal
+// that kernel's bit for bit.
+
+// bf16(float(acc) * xs * ws[n] (+ bias[n])) on both lanes: the store epilogue's value
+__device__ __forceinline__ float2 dequant_bf16x2(uint32_t r0, uint32_t r1, float xs_m, const GemmArgs& a, int n0,
+                                                 int n1) {
+  const float2 w = a.ws_scalar ? make_float2(a.ws[0], a.ws[0]) : make_float2(__ldg(a.ws + n0), __ldg(a.ws + n1));
+  const float2 v = mul2(make_float2((float)(int)r0, (float)(int)r1), splat2(xs_m));
+  return bf16r2(a.bias ? fma2(v, w, make_float2(__ldg(a.bias + n0), __ldg(a.bias + n1))) : mul2(v, w));
+}
+
+// GELU and the first three transform stages of this warp's two blocks, written back
+// over the warp's own accumulator columns
+__device__ __forceinline__ void gelu_rot_first_half(uint32_t taddr, int hh, int nbase, float xs_m,
+                                                    const GemmArgs& a) {
+  const uint32_t tcol = taddr + (uint32_t)(hh * 128);
+  const int ncol = nbase + hh * 128;
+  float2 v[4][16];  // [16-column chunk of the block][column], lanes = (block 2hh, block 2hh + 1)
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t r0[16], r1[16];
+    tmem_ld16(tcol + (uint32_t)(q * 16), r0);
+    tmem_ld16(tcol + (uint32_t)(64 + q * 16), r1);
+    tmem_wait_ld();
+    reg_barrier16(r0);
+    reg_barrier16(r1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = ncol + q * 16 + j;
+      v[q][j] = gelu_tanh2(dequant_bf16x2(r0[j], r1[j], xs_m, a, n, n + 64));
+    }
+    fht16x2(v[q]);  // stride 1 and 4 inside the chunk
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {  // stride 16: the four chunks of the block
+    const float2 x[4] = {v[0][j], v[1][j], v[2][j], v[3][j]};
+    float2 y[4];
+    h4_stage2(x, 1, y, 0);
+    v[0][j] = y[0];
+    v[1][j] = y[1];
+    v[2][j] = y[2];
+    v[3][j] = y[3];
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w0[16], w1[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      w0[j] = __float_as_uint(v[q][j].x);
+      w1[j] = __float_as_uint(v[q][j].y);
+    }
+    tmem_st16(tcol + (uint32_t)(q * 16), w0);
+    tmem_st16(tcol + (uint32_t)(64 + q * 16), w1);
+  }
+  tmem_wait_st();
+}
+
+// The stride-64 stage for positions [32 hh, 32 hh + 32) of the four blocks, the bf16
+// stores and the absmax; releases the accumulator (cluster barrier address tempty)
+// after the last TMEM read.
+__device__ __forceinline__ void gelu_rot_second_half(uint32_t taddr, int hh, int nb, int m, const GemmArgs& a,
+                                                     uint32_t tempty) {
+  float amax = 0.0f;
+  const bool live = m < a.M;
+  uint16_t* dst_row = a.out + (int64_t)(live ? m : 0) * a.out_stride + (int64_t)nb * 256;
+#pragma unroll
+  for (int sub = 0; sub < 2; ++sub) {
+    const int c0 = hh * 32 + sub * 16;
+    uint32_t x[4][16];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) tmem_ld16(taddr + (uint32_t)(b * 64 + c0), x[b]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int b = 0; b < 4; ++b) reg_barrier16(x[b]);
+    if (sub == 1) {
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(tempty);
+    }
+    uint32_t packed[4][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 in[4] = {
+          make_float2(__uint_as_float(x[0][2 * i]), __uint_as_float(x[0][2 * i + 1])),
+          make_float2(__uint_as_float(x[1][2 * i]), __uint_as_float(x[1][2 * i + 1])),
+          make_float2(__uint_as_float(x[2][2 * i]), __uint_as_float(x[2][2 * i + 1])),
+          make_float2(__uint_as_float(x[3][2 * i]), __uint_as_float(x[3][2 * i + 1]))};
+      float2 y[4];
+      h4_stage2(in, 1, y, 0);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        amax = fmaxf(amax, fmaxf(fabsf(y[b].x), fabsf(y[b].y)));
+        packed[b][i] = bf16x2_bits(y[b].x, y[b].y);
+      }
+    }
+    if (live) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        uint4* d = reinterpret_cast<uint4*>(dst_row + b * 64 + c0);
+        d[0] = make_uint4(packed[b][0], packed[b][1], packed[b][2], packed[b][3]);
+        d[1] = make_uint4(packed[b][4], packed[b][5], packed[b][6], packed[b][7]);
+      }
+    }
+  }
+  if (live) a.amax[(int64_t)m * a.amax_stride + 2 * nb + hh] = amax;
+}
 
 // Warp layout of the 2-SM kernel per epilogue kind.  The bf16 epilogues (store,
 // gated residual, q/k norm + RoPE) run 8 epilogue warps, two per TMEM lane
@@ -398,7 +519,7 @@ struct PairSmem {
 template <int KIND>
 struct PairCfg {
   static constexpr bool kQk = KIND == kEpiQkRope64 || KIND == kEpiQkRope48;
-  static constexpr bool kWide = kQk || KIND == kEpiResidual || KIND == kEpiStore;
+  static constexpr bool kWide = kQk || KIND == kEpiResidual || KIND == kEpiStore || KIND == kEpiGeluRot;
   static constexpr int kThreads = kWide ? 384 : kGemmThreads;
   static constexpr int kEpiWarp0 = kWide ? 4 : 2;
   static constexpr int kEpiWarps = kWide ? 8 : 4;
@@ -426,6 +547,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThre
   uint64_t* tempty = tfull + 2;           // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // GELU + ConvRot exchange: [quadrant][half][accumulator], "this half's values are in TMEM"
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -443,6 +566,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThre
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 2 * PairCfg<KIND>::kEpiWarps);
     }
+    if (KIND == kEpiGeluRot)
+      for (int b = 0; b < 16; ++b) mbar_init(&xbar[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -575,6 +700,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<KIND>::kThre
         }
         if (is_q || is_k)
           qk_head_finish<KIND == kEpiQkRope64 ? 64 : 48>(yb, s, m, n_h, is_q ? a.q_norm : a.k_norm, a);
+      } else if constexpr (KIND == kEpiGeluRot) {
+        static_assert(PBN == 256, "one ConvRot group per 256-column tile");
+        const int hh = (warp - PairCfg<KIND>::kEpiWarp0) >> 2;
+        gelu_rot_first_half(taddr, hh, nb * PBN, xs_m, a);
+        // the partner warp's stride-16 results are in its half of the accumulator columns
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xbar[(quad * 2 + hh) * 2 + acc]);
+        if (!mbar_wait_warp(&xbar[(quad * 2 + (hh ^ 1)) * 2 + acc], acc_phase, abort_flag,
+                            H3B_STATUS_GEMM_TIMEOUT))
+          break;
+        tc_fence_after();
+        gelu_rot_second_half(taddr, hh, nb, m, a, tempty0 + (uint32_t)(acc * 8));
       } else if constexpr (PairCfg<KIND>::kWide) {
         // this warp's 128-column half of the tile
         const int hh = (warp - PairCfg<KIND>::kEpiWarp0) >> 2;
@@ -722,11 +860,12 @@ int launch_gemm(const void* A, const void* B, GemmArgs a, int kind, cudaStream_t
                     : kind == kEpiResidual  ? launch_gemm_pair<kEpiResidual>(ta, tb, a, s)
                     : kind == kEpiQkRope64  ? launch_gemm_pair<kEpiQkRope64>(ta, tb, a, s)
                     : kind == kEpiQkRope48  ? launch_gemm_pair<kEpiQkRope48>(ta, tb, a, s)
+                    : kind == kEpiGeluRot   ? launch_gemm_pair<kEpiGeluRot>(ta, tb, a, s)
                                             : launch_gemm_pair<kEpiInt32>(ta, tb, a, s);
     *err = e;
     return e == cudaSuccess ? 0 : 2;
   }
-  if (kind == kEpiQkRope64 || kind == kEpiQkRope48) return 4;
+  if (kind == kEpiQkRope64 || kind == kEpiQkRope48 || kind == kEpiGeluRot) return 4;
   const int tiles256 = ((a.M + kBM - 1) / kBM) * ((a.N + 255) / 256);
   if (kind == kEpiAddF32) {
     // bf16 operands [rows, a.K / 2] (a.K counts bytes); 64 elements = 128 bytes per box row

@@ -383,6 +383,13 @@ __device__ __forceinline__ void reg_barrier32(uint32_t (&r)[32]) {
                  "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
 }
 
+__device__ __forceinline__ void reg_barrier16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
 // layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 bytes, 8-row
 // swizzle atoms of 1024 bytes stacked at a stride of 1024 bytes (SBO).  The

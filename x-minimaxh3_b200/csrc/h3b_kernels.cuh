@@ -20,14 +20,22 @@ struct QuantArgs {
   float eps;
 };
 cudaError_t launch_quant(const QuantArgs& a, int64_t rows, int mode, bool rms, cudaStream_t s);
+// Codes and row scales of rotated bf16 rows [rows, K] whose absmax is spread over
+// amax[row * amax_stride + c], c < amax_cols (the GELU + ConvRot GEMM epilogue's output)
+cudaError_t launch_quant_rotated(const uint16_t* rot, int64_t rot_stride, const float* amax, int64_t amax_stride,
+                                 int amax_cols, int K, int64_t rows, int8_t* q, float* scales, cudaStream_t s);
 int quant_threads_for(int K);
 
 // kEpiQkRope64 / 48: the store epilogue of the QKV projection with the per-head q/k
 // RMSNorm and split-half RoPE (rotary half-width 64 or 48) applied before the store
 // kEpiAddF32: bf16 x bf16 operands (kind::f16, K in bytes = 2 x elements), the fp32
 // product added into the bf16 output in place: D = bf16(float(D) + acc)
+// kEpiGeluRot: the store epilogue's bf16 values through tanh-GELU and the 256-point
+// ConvRot transform (one group per 256-column tile), stored as bf16, with the fp32
+// absmax of each (row, tile, half) written to amax[m * amax_stride + 2 * tile + half];
+// half h covers the tile's columns 64 j + 32 h + [0, 32), j = 0..3
 enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiInt32 = 2, kEpiQkRope64 = 3, kEpiQkRope48 = 4,
-                     kEpiAddF32 = 5 };
+                     kEpiAddF32 = 5, kEpiGeluRot = 6 };
 struct GemmArgs {
   int M, N, K;
   const float* xs;
@@ -47,6 +55,9 @@ struct GemmArgs {
   const uint16_t* cos_t;
   const uint16_t* sin_t;
   float qk_eps;
+  // GELU + ConvRot epilogue: per-(row, half-tile) absmax of the rotated values
+  float* amax;
+  int64_t amax_stride;
 };
 // True when an M x N GEMM runs the 2-SM kernel (the only one with the q/k epilogue).
 bool gemm_uses_pair_kernel(int64_t M, int64_t N);

@@ -17,20 +17,13 @@
 // along a column (in registers).  The operation order inside each radix-4
 // butterfly is the reference's, so results equal its fp32 transform bit for bit.
 #include "h3b_kernels.cuh"
+#include "h3b_packed.cuh"
 
 namespace h3b {
 
 enum QuantMode : int { kPlain = 0, kConvRot = 1 };
 
 
-
-// int8 code of a scaled value s: clamp to [-128, 127], round half to even by
-// adding 1.5 * 2^23, and take the low byte of the sum's bits -- the code of
-// rintf + clamp + (int) (clamping first cannot change the rounded result).
-__device__ __forceinline__ uint32_t code_byte(float s) {
-  const float c = fminf(127.0f, fmaxf(-128.0f, s));
-  return __float_as_uint(__fadd_rn(c, 12582912.0f)) & 0xffu;
-}
 
 // Warp shfl_down tree then the same tree over the (zero padded) warp sums:
 // identical to block_tree_sum in the CPU oracle.
@@ -68,109 +61,6 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   }
   __syncthreads();
   return red[32];
-}
-
-// ---------------------------------------------------------------- packed pairs
-// Every thread owns chunk i of two neighbouring 256-column groups (chunks
-// 32p + i and 32p + 16 + i, p = thread / 16, i = thread % 16) and keeps the two
-// as the lanes of float2 values, so the per-element arithmetic runs as packed
-// FFMA2 / FADD2 / FMUL2 -- IEEE round-to-nearest per lane, the same bits as the
-// scalar operations -- and both lanes take the same place in their groups'
-// 16 x 16 transform arrays.
-__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
-// a - b with one rounding: b * -1 is exact, so the fused product-add rounds a - b
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
-// both lanes rounded to bf16 (cvt.rn.bf16x2.f32) and widened back
-__device__ __forceinline__ float2 bf16r2(float2 v) {
-  uint32_t p;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v.y), "f"(v.x));
-  return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
-}
-__device__ __forceinline__ float2 div2_rn_by(float2 a, float2 b, float2 rb) {
-  const float2 q = mul2(a, rb);
-  const float2 r = fma2(q, make_float2(-b.x, -b.y), a);
-  return fma2(r, rb, q);
-}
-
-// One radix-4 butterfly of the regular H4 matrix on both lanes, outputs in the
-// reference's operation order (int8_linear.cu:217-250): y0 = ((x0+x1)+x2)-x3,
-// y1 = ((x0+x1)-x2)+x3, y2 = ((x0-x1)+x2)+x3, y3 = ((-x0+x1)+x2)+x3, times 1/2.
-// x0+x1 and x0-x1 are shared; (-x0+x1)+x2 == x2-(x0-x1) exactly.
-__device__ __forceinline__ void h4_stage2(const float2* x, int s, float2* y, int base) {
-  const float2 h = splat2(0.5f);
-  const float2 x0 = x[base], x1 = x[base + s], x2 = x[base + 2 * s], x3 = x[base + 3 * s];
-  const float2 s01 = add2(x0, x1), d01 = sub2(x0, x1);
-  y[base] = mul2(h, sub2(add2(s01, x2), x3));
-  y[base + s] = mul2(h, add2(sub2(s01, x2), x3));
-  y[base + 2 * s] = mul2(h, add2(add2(d01, x2), x3));
-  y[base + 3 * s] = mul2(h, add2(sub2(x2, d01), x3));
-}
-// Two radix-4 stages (stride 1 then 4) over the 16 values of each lane.
-__device__ __forceinline__ void fht16x2(float2 (&v)[16]) {
-  float2 t[16];
-#pragma unroll
-  for (int b0 = 0; b0 < 16; b0 += 4) h4_stage2(v, 1, t, b0);
-#pragma unroll
-  for (int b0 = 0; b0 < 4; ++b0) h4_stage2(t, 4, v, b0);
-}
-
-// exp(x) for x in [-20, 0], the argument range of the GELU's tanh, on both
-// lanes: the IEEE operations of h3b_expf on that range without its range
-// branches.  rint(x log2 e) is taken by adding and subtracting 1.5 * 2^23 (round
-// half to even, as rintf), the integer exponent comes from that sum's low bits,
-// and one power-of-two scaling replaces the two half scalings (equal, since every
-// product stays normal for n >= -29).  Matches h3b_expf bit for bit on every
-// float of [-20, 0].
-__device__ __forceinline__ float2 expf_neg20x2(float2 x) {
-  const float kLog2e = 1.44269502162933349609375f;
-  const float kLn2Hi = 0.693145751953125f;
-  const float kLn2Lo = 1.428606765330187045e-06f;
-  const float2 t = add2(mul2(x, splat2(kLog2e)), splat2(12582912.0f));
-  const float2 n = sub2(t, splat2(12582912.0f));
-  float2 r = fma2(n, splat2(-kLn2Hi), x);
-  r = fma2(n, splat2(-kLn2Lo), r);
-  float2 p = splat2(1.0f / 5040.0f);
-  p = fma2(p, r, splat2(1.0f / 720.0f));
-  p = fma2(p, r, splat2(1.0f / 120.0f));
-  p = fma2(p, r, splat2(1.0f / 24.0f));
-  p = fma2(p, r, splat2(1.0f / 6.0f));
-  p = fma2(p, r, splat2(0.5f));
-  p = fma2(p, r, splat2(1.0f));
-  p = fma2(p, r, splat2(1.0f));
-  const int nx = (int)(__float_as_uint(t.x) - 0x4B400000u), ny = (int)(__float_as_uint(t.y) - 0x4B400000u);
-  return mul2(p, make_float2(__uint_as_float((uint32_t)(nx + 127) << 23), __uint_as_float((uint32_t)(ny + 127) << 23)));
-}
-// RN(1 / d) for d in [1, 2]: the approximate reciprocal refined by one Newton
-// step, y + y (1 - d y).  Checked against the IEEE reciprocal (__frcp_rn) on
-// every float of [1, 2] on B200: identical bits.
-__device__ __forceinline__ float2 rcp2_1to2(float2 d) {
-  float yx, yy;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yx) : "f"(d.x));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yy) : "f"(d.y));
-  const float2 y = make_float2(yx, yy);
-  return fma2(fma2(make_float2(-d.x, -d.y), y, splat2(1.0f)), y, y);
-}
-// GELU (tanh form) on both lanes.  tanh(x) = sign(x) (1 - e) / (1 + e), e =
-// exp(-2|x|): the quotient is correctly rounded by Markstein's final step from
-// RN(1 / (1 + e)) (equal to IEEE division for every e in [2e-9, 1], the range
-// exp(-2|x|) takes for |x| < 10).  The exponent is clamped at -20, so |x| >= 10
-// gives e = exp(-20), 1 - e and 1 + e both round to 1 and tanh = +-1 exactly; the
-// sign is the sign bit of x (t >= 0; a -0 only ever reaches 1 + t).
-__device__ __forceinline__ float2 gelu_tanh2(float2 v) {
-  const float kBeta = 0.7978845608028654f;
-  const float kKappa = 0.044715f;
-  const float2 cube = mul2(mul2(mul2(splat2(kKappa), v), v), v);
-  const float2 x = mul2(splat2(kBeta), add2(v, cube));
-  const float2 m2a = mul2(splat2(-2.0f), make_float2(fabsf(x.x), fabsf(x.y)));
-  const float2 e = expf_neg20x2(make_float2(fmaxf(m2a.x, -20.0f), fmaxf(m2a.y, -20.0f)));
-  const float2 num = sub2(splat2(1.0f), e), den = add2(splat2(1.0f), e);
-  float2 t = div2_rn_by(num, den, rcp2_1to2(den));
-  t.x = __uint_as_float(__float_as_uint(t.x) | (__float_as_uint(x.x) & 0x80000000u));
-  t.y = __uint_as_float(__float_as_uint(t.y) | (__float_as_uint(x.y) & 0x80000000u));
-  return mul2(mul2(splat2(0.5f), v), add2(splat2(1.0f), t));
 }
 
 // h3b_expf on both lanes.  For rint(x log2 e) = n in [-125, 127] (|x| below ~86)
@@ -242,13 +132,6 @@ __device__ __forceinline__ void load_row(const QuantArgs& a, int64_t row, int cx
   const uint16_t* xr = a.x + row * a.x_stride;
   load_pair(xr, cx, cy, lx, ly, r.x[0], r.x[1]);
   if (ACT == 2) load_pair(xr + a.K, cx, cy, lx, ly, r.u[0], r.u[1]);
-}
-
-// int8 codes of both lanes: the scalar code_byte(bf16(bf16(v) / st)) lane by lane
-__device__ __forceinline__ void codes2(float2 v, float2 st2, float2 rst2, uint32_t& bx, uint32_t& by) {
-  const float2 d = bf16r2(div2_rn_by(bf16r2(v), st2, rst2));
-  bx = code_byte(d.x);
-  by = code_byte(d.y);
 }
 
 // Persistent: CTA b handles rows b, b + gridDim.x, ...; the next row's loads are
@@ -373,6 +256,72 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t ro
       if (ly) *reinterpret_cast<uint4*>(qr + cy * 16) = make_uint4(py[0], py[1], py[2], py[3]);
     }
   }
+}
+
+// ---------------------------------------------------------------- rotated rows -> codes
+// The second half of the FC2 input quantizer when FC1's GEMM epilogue has already
+// applied tanh-GELU and the ConvRot transform: per row, the absmax is the max of the
+// epilogue's per-(row, half-tile) maxima, and the codes are formed from the stored
+// bf16 rotated values exactly as quant_rows_kernel forms them from its fp32 ones
+// (code of bf16(bf16(v) / bf16(scale))).  One CTA per row at a time (persistent);
+// thread t owns the 8-column chunks t, t + 256, ... (16-byte loads, 8-byte stores).
+constexpr int kRotThreads = 256;
+constexpr int kRotMaxChunks = 8;  // K <= 8 * 8 * 256 = 16384 in registers
+__global__ void __launch_bounds__(kRotThreads) quant_rotated_kernel(const uint16_t* __restrict__ rot,
+                                                                    int64_t rot_stride, const float* __restrict__ amax,
+                                                                    int64_t amax_stride, int amax_cols, int K,
+                                                                    int64_t rows, int8_t* __restrict__ q,
+                                                                    float* __restrict__ scales) {
+  __shared__ float red[33];
+  const int t = threadIdx.x;
+  const int chunks = K >> 3;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const uint16_t* src = rot + row * rot_stride;
+    uint4 w[kRotMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kRotMaxChunks; ++i) {
+      const int c = t + i * kRotThreads;
+      w[i] = c < chunks ? __ldg(reinterpret_cast<const uint4*>(src) + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float am = 0.0f;
+    for (int c = t; c < amax_cols; c += kRotThreads) am = fmaxf(am, __ldg(amax + row * amax_stride + c));
+    am = block_max(am, red);
+    const float scale = fmaxf(__fmul_rn(fminf(am, 3.38953139e38f), 1.0f / 127.0f), 1.0e-30f);
+    const float st = bf16r(scale);
+    const float2 st2 = splat2(st), rst2 = splat2(__fdiv_rn(1.0f, st));
+    if (t == 0) scales[row] = scale;
+    int8_t* dst = q + row * (int64_t)K;
+#pragma unroll
+    for (int i = 0; i < kRotMaxChunks; ++i) {
+      const int c = t + i * kRotThreads;
+      if (c >= chunks) continue;
+      const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t b0, b1;
+        codes2(make_float2(__uint_as_float(ww[j] << 16), __uint_as_float(ww[j] & 0xffff0000u)), st2, rst2, b0, b1);
+        const uint32_t pair = b0 | (b1 << 8);
+        if (j < 2) lo |= pair << (16 * j);
+        else hi |= pair << (16 * (j - 2));
+      }
+      *reinterpret_cast<uint2*>(dst + c * 8) = make_uint2(lo, hi);
+    }
+  }
+}
+
+cudaError_t launch_quant_rotated(const uint16_t* rot, int64_t rot_stride, const float* amax, int64_t amax_stride,
+                                 int amax_cols, int K, int64_t rows, int8_t* q, float* scales, cudaStream_t s) {
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quant_rotated_kernel, kRotThreads, 0);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t cap = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+  const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+  quant_rotated_kernel<<<grid, kRotThreads, 0, s>>>(rot, rot_stride, amax, amax_stride, amax_cols, K, rows, q, scales);
+  return cudaGetLastError();
 }
 
 // Threads per row: 16 per pair of 256-column groups (chunk pairs), rounded up to

@@ -59,6 +59,10 @@ _SIGNATURES = {
     "h3b_int8_gemm_gated_residual": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                      c_int64, c_int64, c_int64, c_int64, c_void_p],
     "h3b_int8_gemm_i32": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p],
+    "h3b_int8_gemm_gelu_convrot": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+                                   c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p],
+    "h3b_quantize_rotated_int8": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+                                  c_void_p, c_void_p],
     "h3b_dequant_int4_grouped_to_int8": [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                          c_void_p],
     "h3b_w4a8_group_sums": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p],

@@ -12,8 +12,12 @@ Per block (model/layers.py:1074-1298, fused_mlp.py:269-426):
   [all-to-all heads -> tokens]
   x += gate_a * INT8 GEMM(ConvRot INT8(o))    h3b_quantize_int8_rowwise_convrot + gated-residual GEMM
   xq = rms_adaln + ConvRot + INT8(x)
-  h = W4A8 GEMM(xq, W_fc1) + bias             h3b_dequant_int4_grouped_to_int8 + GEMM
-  x += gate_m * W4A8 GEMM(gelu/swiglu + ConvRot INT8(h), W_fc2)
+  h = W4A8 GEMM(xq, W_fc1) + bias,            h3b_dequant_int4_grouped_to_int8 +
+    gelu + ConvRot in the epilogue            h3b_int8_gemm_gelu_convrot, then
+  hq = INT8(h)                                h3b_quantize_rotated_int8 (swiglu, or
+                                              shapes the fused epilogue does not take:
+                                              GEMM + h3b_quantize_int8_rowwise_convrot)
+  x += gate_m * W4A8 GEMM(hq, W_fc2)          gated-residual GEMM
 
 Weights are random-initialised with the checkpoint formats the reference loads
 (per-output-channel INT8, grouped packed INT4 with fp32 s_rel and s_channel).
@@ -310,9 +314,7 @@ class DiTBlockB200:
             seg_i = _chunk_segments(segments, r0, r1)
             xq, xs = ops.rms_adaln_quantize_int8(x[r0:r1], self.norm2, scale_m, shift_m, seg_i, cfg.eps,
                                                  self.fc1.convrot_group_size)
-            h = self.fc1.forward_prequantized(xq, xs)
-            hq, hs = self.fc2.quantize(h, cfg.mlp_act)
-            del h
+            hq, hs = self.fc1.forward_prequantized_for(self.fc2, xq, xs, cfg.mlp_act)
             self._gated(self.fc2, x[r0:r1], gate_m, hq, hs, _runs(seg_i, r1 - r0, mod.shape[0]))
             if rows_done is not None:
                 rows_done(i)

@@ -259,6 +259,56 @@ def int8_linear_prequantized_qk_rope(xq: torch.Tensor, xs: torch.Tensor, weight:
     return qk_rmsnorm_rope_(out, heads, q_offset, k_offset, qw, kw, ct, st, eps)
 
 
+def quantize_rotated_int8(rot: torch.Tensor, amax: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row INT8 codes and scales of GELU + ConvRot rotated bf16 rows whose absmax is
+    spread over amax [M, C] (the output of the fused FC1 epilogue)."""
+    _cuda("quantize_rotated_int8", rot, amax)
+    if rot.dtype != torch.bfloat16 or rot.ndim != 2 or rot.stride(1) != 1:
+        raise ValueError("rot must be bfloat16 rows [M, K] with unit column stride")
+    if amax.dtype != torch.float32 or amax.ndim != 2 or amax.shape[0] != rot.shape[0] or amax.stride(1) != 1:
+        raise ValueError("amax must be float32 [M, C] with unit column stride")
+    M, K = rot.shape
+    q = torch.empty((M, K), device=rot.device, dtype=torch.int8)
+    s = torch.empty((M, 1), device=rot.device, dtype=torch.float32)
+    check(lib().h3b_quantize_rotated_int8(_p(rot), M, K, rot.stride(0), _p(amax), amax.stride(0), amax.shape[1],
+                                          _p(q), _p(s), _stream(rot)), "quantize_rotated_int8")
+    return q, s
+
+
+def int8_linear_gelu_convrot_quantize(xq: torch.Tensor, xs: torch.Tensor, weight: torch.Tensor,
+                                      weight_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                                      ) -> tuple[torch.Tensor, torch.Tensor]:
+    """FC1 of the GELU MLP and the next layer's input quantizer (tanh-GELU, ConvRot-256,
+    per-row INT8) in two launches: the GEMM epilogue applies the GELU and the rotation,
+    a light pass forms the codes (model/fused_mlp.py:269-426 with comfy_kitchen
+    int8_linear.cu:943-1030).  Bit-identical to int8_linear_prequantized followed by
+    quantize_int8_rowwise_convrot64(h, 256, "gelu_tanh"), which it runs instead when
+    the library reports the shape unsupported by the fused epilogue (GEMMs that take
+    the 1-SM kernel, widths that are not a multiple of 256 or above 16384)."""
+    _cuda("int8_linear_gelu_convrot_quantize", xq, xs, weight)
+    if weight.dtype != torch.int8 or weight.ndim != 2:
+        raise ValueError("weight must be a rank-two int8 tensor")
+    xq2 = xq if xq.is_contiguous() else xq.contiguous()
+    M, K = xq2.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise ValueError(f"Input and weight inner dimensions must match, got {K} and {weight.shape[1]}")
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    ws = _weight_scale(weight_scale, N, xq.device)
+    b = _bias_f32(bias, N, xq.device)
+    xs2 = xs.reshape(-1).to(torch.float32).contiguous()
+    rot = torch.empty((M, N), device=xq.device, dtype=torch.bfloat16)
+    amax = torch.empty((M, max(N // 128, 1)), device=xq.device, dtype=torch.float32)
+    status = lib().h3b_int8_gemm_gelu_convrot(_p(xq2), _p(w), _p(xs2), _p(ws), ws.numel(), _p(b), _p(rot), M, N, K,
+                                              rot.stride(0), _p(amax), amax.stride(0), _stream(xq))
+    if status != H3B_ERR_UNSUPPORTED:
+        check(status, "int8_linear_gelu_convrot_quantize")
+        return quantize_rotated_int8(rot, amax)
+    del amax
+    int8_linear_prequantized(xq2, xs2, w, ws, b, out=rot)
+    return quantize_int8_rowwise_convrot64(rot, 256, "gelu_tanh")
+
+
 def _quantize_for_linear(x, convrot, convrot_groupsize, input_act):
     if convrot:
         return quantize_int8_rowwise_convrot64(x, convrot_groupsize, input_act)

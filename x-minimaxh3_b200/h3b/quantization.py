@@ -140,6 +140,20 @@ class _QuantLinear:
         self._correct_(out, xq, xs)
         return out
 
+    def forward_prequantized_for(self, next_layer: "_QuantLinear", xq: torch.Tensor, xs: torch.Tensor,
+                                 input_act: str | None) -> tuple[torch.Tensor, torch.Tensor]:
+        """This layer's output quantized as `next_layer`'s input with `input_act` applied
+        (the MLP's FC1 feeding FC2, model/fused_mlp.py:269-426).  With a ConvRot next
+        layer, tanh-GELU and no post-GEMM correction on this layer, the activation and
+        the rotation run in this GEMM's epilogue; the codes and scales are the same
+        either way."""
+        if (input_act == "gelu_tanh" and next_layer.spec_convrot
+                and getattr(self, "correction", None) is None):
+            w8, ws = self.int8_weight()
+            return ops.int8_linear_gelu_convrot_quantize(xq, xs, w8, ws, self.bias)
+        h = self.forward_prequantized(xq, xs)
+        return next_layer.quantize(h, input_act)
+
     def forward_prequantized_qk_rope(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor, heads: int,
                                      q_offset: int, k_offset: int, q_weight: torch.Tensor, k_weight: torch.Tensor,
                                      cos_table: torch.Tensor, sin_table: torch.Tensor, eps: float) -> torch.Tensor:
