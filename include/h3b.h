@@ -138,8 +138,8 @@ int h3b_int8_gemm_dequant_qk_rope(const void* A, const void* B, const void* xs, 
  * h3b_quantize_rotated_int8 forms the codes and row scales, bit-identical to
  * h3b_int8_gemm_dequant followed by h3b_quantize_int8_rowwise_convrot(input_act = 1).
  * Returns H3B_ERR_UNSUPPORTED with nothing launched unless the shape runs the 2-SM
- * kernel (ceil(M/256) * ceil(N/256) >= the SM count), N % 256 == 0, N <= 16384, D is
- * 16-byte aligned with out_row_stride % 8 == 0 and amax_row_stride >= N / 128; the
+ * kernel (ceil(M/256) * ceil(N/256) >= the SM count), N % 256 == 0, N <= 16384, D, ws
+ * and bias are 16-byte aligned with out_row_stride % 8 == 0 and amax_row_stride >= N / 128; the
  * caller then makes those two calls.  Replaces the FC1 projection followed by the
  * FC2 input quantizer with input_act gelu_tanh (model/fused_mlp.py:269-426 feeding
  * comfy_kitchen int8_linear.cu:943-1030). */

@@ -207,8 +207,9 @@ int h3b_int8_gemm_gelu_convrot(const void* A, const void* B, const void* xs, con
     return fail(H3B_ERR_INVALID_ARGUMENT, "out_row_stride < N or amax_row_stride < N / 128");
   if (N % 256 || N > 16384)
     return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: need N % 256 == 0 and N <= 16384");
-  if (!aligned16(D) || out_row_stride % 8)
-    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: D must be 16-byte aligned, out_row_stride % 8 == 0");
+  if (!aligned16(D) || out_row_stride % 8 || !aligned16(ws) || (bias && !aligned16(bias)))
+    return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: D, ws and bias must be 16-byte aligned, "
+                                     "out_row_stride % 8 == 0");
   if (M > 0 && N > 0 && !h3b::gemm_uses_pair_kernel(M, N))
     return fail(H3B_ERR_UNSUPPORTED, "int8_gemm_gelu_convrot: the shape does not run the 2-SM kernel");
   h3b::GemmArgs g{};

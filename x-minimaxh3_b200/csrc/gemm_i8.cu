@@ -403,11 +403,14 @@ struct PairSmem {
 // that kernel's bit for bit.
 
 // bf16(float(acc) * xs * ws[n] (+ bias[n])) on both lanes: the store epilogue's value
-__device__ __forceinline__ float2 dequant_bf16x2(uint32_t r0, uint32_t r1, float xs_m, const GemmArgs& a, int n0,
-                                                 int n1) {
-  const float2 w = a.ws_scalar ? make_float2(a.ws[0], a.ws[0]) : make_float2(__ldg(a.ws + n0), __ldg(a.ws + n1));
+__device__ __forceinline__ float2 dequant_bf16x2(uint32_t r0, uint32_t r1, float xs_m, float2 w, float2 b,
+                                                 bool has_bias) {
   const float2 v = mul2(make_float2((float)(int)r0, (float)(int)r1), splat2(xs_m));
-  return bf16r2(a.bias ? fma2(v, w, make_float2(__ldg(a.bias + n0), __ldg(a.bias + n1))) : mul2(v, w));
+  return bf16r2(has_bias ? fma2(v, w, b) : mul2(v, w));
+}
+// four consecutive per-column values (16-byte aligned: n is a multiple of 4)
+__device__ __forceinline__ float4 ld_col4(const float* p, int n) {
+  return __ldg(reinterpret_cast<const float4*>(p + n));
 }
 
 // GELU and the first three transform stages of this warp's two blocks, written back
@@ -426,9 +429,20 @@ __device__ __forceinline__ void gelu_rot_first_half(uint32_t taddr, int hh, int 
     reg_barrier16(r0);
     reg_barrier16(r1);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int n = ncol + q * 16 + j;
-      v[q][j] = gelu_tanh2(dequant_bf16x2(r0[j], r1[j], xs_m, a, n, n + 64));
+    for (int j4 = 0; j4 < 16; j4 += 4) {
+      const int n = ncol + q * 16 + j4;
+      const float4 w0 = a.ws_scalar ? make_float4(a.ws[0], a.ws[0], a.ws[0], a.ws[0]) : ld_col4(a.ws, n);
+      const float4 w1 = a.ws_scalar ? w0 : ld_col4(a.ws, n + 64);
+      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 b0 = a.bias ? ld_col4(a.bias, n) : zero;
+      const float4 b1 = a.bias ? ld_col4(a.bias, n + 64) : zero;
+      const float2 w[4] = {make_float2(w0.x, w1.x), make_float2(w0.y, w1.y), make_float2(w0.z, w1.z),
+                           make_float2(w0.w, w1.w)};
+      const float2 b[4] = {make_float2(b0.x, b1.x), make_float2(b0.y, b1.y), make_float2(b0.z, b1.z),
+                           make_float2(b0.w, b1.w)};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[q][j4 + j] = gelu_tanh2(dequant_bf16x2(r0[j4 + j], r1[j4 + j], xs_m, w[j], b[j], a.bias != nullptr));
     }
     fht16x2(v[q]);  // stride 1 and 4 inside the chunk
   }

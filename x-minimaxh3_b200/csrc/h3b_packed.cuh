@@ -85,8 +85,11 @@ __device__ __forceinline__ float2 expf_neg20x2(float2 x) {
   p = fma2(p, r, splat2(0.5f));
   p = fma2(p, r, splat2(1.0f));
   p = fma2(p, r, splat2(1.0f));
-  const int nx = (int)(__float_as_uint(t.x) - 0x4B400000u), ny = (int)(__float_as_uint(t.y) - 0x4B400000u);
-  return mul2(p, make_float2(__uint_as_float((uint32_t)(nx + 127) << 23), __uint_as_float((uint32_t)(ny + 127) << 23)));
+  // p * 2^n as one integer add of n << 23 to p's bits (p in [0.7, 1.42], n >= -29: the
+  // product is normal, so this is the exact power-of-two scaling); the magic sum's
+  // bits shifted left by 23 are n << 23 in two's complement
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 // RN(1 / d) for d in [1, 2]: the approximate reciprocal refined by one Newton
 // step, y + y (1 - d y).  Checked against the IEEE reciprocal (__frcp_rn) on
