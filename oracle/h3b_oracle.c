@@ -902,7 +902,7 @@ static float attn_exp2(float x) {
  *   tmax  = max over the step's groups of (max_j v_j - 1.5 * 2^23) * c
  *   m     = tmax if tmax > m + 2 else m (lazy running max); alpha = 2^(m_old - m)
  *   x_j   = fma(v_j, c, (log2 112 - m) - 1.5 * 2^23 * c)
- *   P_j   = 2^x_j: the polynomial above on columns 6, 7 of every 8 of a block,
+ *   P_j   = 2^x_j: the polynomial above on columns 6, 7 of every 16 of a block,
  *           ex2 (hardware, modelled by a correctly rounded exp2) on the others
  *   l     = l * alpha + (sum of the step's fp32 P_j in the kernel's order)
  *   O     = O * alpha + sum_j E4M3(P_j) * E4M3(V_j) * (accumulated in double here;
@@ -986,7 +986,7 @@ void h3bo_attention_kernel(const int8_t* q, const float* qscale, int q_gran, int
                         for (int cidx = 0; cidx < 64; ++cidx) {
                             const int g = k_gran == 1 ? (cidx % 8) / 2 : 0;
                             const float x = fmaf(v[u][cidx], c[u][g], oo[g]);
-                            const int poly = (cidx % 8) == 6 || (cidx % 8) == 7;
+                            const int poly = (cidx % 16) == 6 || (cidx % 16) == 7;
                             p[cidx] = poly ? attn_exp2_poly(x) : attn_exp2(x);
                         }
                         /* the kernel's order: four fp32 accumulators over packed pairs */

@@ -12,7 +12,7 @@
 //       m is a lazily updated running max: it moves (to the tile max) only when
 //       a tile's scores exceed it by more than kTau = 2, so P <= 2^kTau * 112 =
 //       448, the E4M3 maximum, and the O rescale in tensor memory is rare.
-//       Three columns in four take ex2.approx (MUFU), the fourth a polynomial
+//       Seven columns in eight take ex2.approx (MUFU), the eighth a polynomial
 //       on the FMA pipe (packed fp32 pairs), which balances the two pipes.
 //   O += P . V          tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32, tensor memory)
 //   out = O / l * v_scale[d] -> bf16, l the fp32 row sum of P
@@ -28,10 +28,8 @@
 //   warp 1      TMEM allocator
 //   warps 2, 3  MMA issuers of tiles A and B (warp-wide loop over the step
 //               schedule, descriptors in uniform registers, one elected lane
-//               issues): at each of its tile's steps, S(step) as soon as the
-//               softmax has read and re-biased the previous step's scores (so
-//               S runs during the softmax's exponentials), then PV(previous
-//               step) once the previous P is written.
+//               issues): at each of its tile's steps, once the previous P is
+//               written, S(step) and PV(previous step)
 //               P is double-buffered per tile in shared memory.
 //   warps 4..7  softmax of tile A, warps 8..11 of tile B: one query row per
 //               thread (its TMEM lane): S row from TMEM, per-block dequant
@@ -55,6 +53,7 @@ constexpr int kLaunchRegs = 168;
 constexpr int kCtrlRegs = 72;
 constexpr int kSoftmaxRegs = 216;
 static_assert(128 * (kCtrlRegs + 2 * kSoftmaxRegs) <= kAttnThreads * kLaunchRegs, "register split too large");
+constexpr int kTileThreads = 128;
 constexpr int kKVStages = 4;
 constexpr int kQBytes = 128 * 128;
 constexpr int kPBytes = 128 * 128;
@@ -260,9 +259,9 @@ __device__ __forceinline__ void raw_max_ragged_g(uint32_t (&s)[128], int n, int 
 }
 
 // P = 2^(S * cc + oo) over columns [CB, CB + 64), written back as floats, on
-// packed fp32 pairs (FFMA2 / FADD2).  Of every 8 columns, 6 take ex2.approx
-// (MUFU) and 2 (columns 6 and 7) the polynomial exponential on the FMA pipe (the
-// split measured fastest against 2, 6 and 8 in 16 columns); returns the sum.
+// packed fp32 pairs (FFMA2 / FADD2).  Of every 16 columns, 14 take ex2.approx
+// (MUFU) and 2 the polynomial exponential on the FMA pipe (the split measured
+// fastest against 1 in 4, 1 in 16 and none); returns the sum.
 // KG = 4 (per_thread K scales): pair k of each 8-column chunk is scale group k.
 template <int CB, int KG>
 __device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)[KG], const float (&oo)[KG]) {
@@ -286,7 +285,9 @@ __device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)
                         c2[KG == 1 ? 0 : k], o2[KG == 1 ? 0 : k]);
 #pragma unroll
     for (int k = 0; k < 3; ++k) p[k] = make_float2(ex2(x[k].x), ex2(x[k].y));
-    {
+    if ((c >> 3) & 1) {
+      p[3] = make_float2(ex2(x[3].x), ex2(x[3].y));
+    } else {
       // 2^x = 2^j * 2^f, j = rint(x) (low bits of t), f = x - j (exact)
       const float2 xp = make_float2(fmaxf(x[3].x, -125.0f), fmaxf(x[3].y, -125.0f));
       const float2 t = __fadd2_rn(xp, kM);
@@ -337,8 +338,7 @@ __device__ __forceinline__ void rebias_s(uint32_t s_addr) {
 
 // One key pair (or a single trailing block, NC = 64) for one query row of one
 // tile.  The second block's scores load from TMEM while the first block's
-// maximum is taken; once the scores are in registers and the S columns
-// re-biased, s_free lets the MMA warp start the next step's S.  The running max m moves (to the tile max) only when the
+// maximum is taken.  The running max m moves (to the tile max) only when the
 // tile max exceeds it by more than kTau; then O is rescaled.  cnt = steps this
 // tile already processed: the PV of step cnt - 1 may still be running and is
 // waited for, on pv_done, only before O is rescaled.  P is double-buffered: the
@@ -347,8 +347,7 @@ __device__ __forceinline__ void rebias_s(uint32_t s_addr) {
 template <int NC, int KG>
 __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint8_t* prow, int r,
                                              const float (&c0)[KG], const float (&c1)[KG], int n0, int n1, int cnt,
-                                             float& m, float& l, uint64_t* pv_done, uint64_t* s_free,
-                                             volatile int* abort_flag) {
+                                             float& m, float& l, uint64_t* pv_done, volatile int* abort_flag) {
   uint32_t s[128];
   __syncwarp();
   tmem_ld32(s_addr, H3B_S32(s, 0));
@@ -416,12 +415,6 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
 #pragma unroll
   for (int g = 0; g < KG; ++g) o0[g] = off - kMagicF * c0[g];
   float psum = exp_block<0, KG>(s, c0, o0);
-  // the S columns are read and re-biased (the stores had the first block's exponentials
-  // to complete): the next step's S MMA may run during the rest of this step
-  tmem_wait_st();
-  tc_fence_before();
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(s_free);
   if constexpr (NC == 128) {
     float o1[KG];
 #pragma unroll
@@ -429,6 +422,7 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
     psum += exp_block<64, KG>(s, c1, o1);
   }
   store_p<NC>(s, prow, r);
+  tmem_wait_st();
   fence_proxy_async_smem();
   tc_fence_before();
   l = l * alpha + psum;
@@ -448,10 +442,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* kv_empty = kv_full + kKVStages;  // kKVStages
   uint64_t* s_full = kv_empty + kKVStages;   // 2 (per tile): S MMA done
   uint64_t* pv_done = s_full + 2;            // 2 (per tile): PV MMA done
-  uint64_t* p_full = pv_done + 2;            // 2 (per tile, one arrival per softmax warp): P written
+  uint64_t* p_full = pv_done + 2;            // 2 (per tile, 128 arrivals): P written, S read
   uint64_t* o_full = p_full + 2;             // 2 (per tile)
-  uint64_t* s_free = o_full + 2;             // 2 (per tile, one arrival per softmax warp): S read
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -469,12 +462,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&pv_done[t], 1);
-      mbar_init(&p_full[t], 4);
+      mbar_init(&p_full[t], kTileThreads);
     }
     mbar_init(&o_full[0], 1);
     mbar_init(&o_full[1], 1);
-    mbar_init(&s_free[0], 4);
-    mbar_init(&s_free[1], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -562,16 +553,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool ptwo = false, first = true;
     uint32_t pbuf = 0;     // P buffer of the pending PV
     uint32_t ppar = 0;     // parity of the next p_full phase
-    uint32_t spar = 0;     // parity of the next s_free phase
     auto wait_p = [&]() -> bool {
       if (!mbar_wait_warp(&p_full[t], ppar, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
       ppar ^= 1u;
-      tc_fence_after();
-      return true;
-    };
-    auto wait_s = [&]() -> bool {
-      if (!mbar_wait_warp(&s_free[t], spar, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
-      spar ^= 1u;
       tc_fence_after();
       return true;
     };
@@ -599,9 +583,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       if ((who >> t) & 1) {
         const bool two = j1 >= 0;
-        // S of this step reuses the S columns: the previous step's scores must be read
-        // (the softmax re-biases them before its exponentials, so this S overlaps those)
-        if (pst >= 0 && !wait_s()) { ok = false; break; }
+        // S of this step reuses the S columns: the previous P must be written
+        if (pst >= 0 && !wait_p()) { ok = false; break; }
         const uint64_t kdesc = sdesc_kmajor_sw128(kv_addr + (uint32_t)(stage * kKVBytes));
         const uint32_t idesc_s = two ? idesc_i8(128, 128) : idesc_i8(128, 64);
         if (elect_one()) {
@@ -610,10 +593,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mma_commit(&s_full[t]);
         }
         __syncwarp();
-        if (pst >= 0) {
-          if (!wait_p()) { ok = false; break; }
-          issue_pv();
-        }
+        if (pst >= 0) issue_pv();
         pst = stage;
         ptwo = two;
         if (!it.pending(t)) {
@@ -684,14 +664,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       uint8_t* prow = prow0 + (cnt & 1) * kPBytes;
       ok = two ? softmax_step<128, KG>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
-                                       &s_free[t], abort_flag)
+                                       abort_flag)
                : softmax_step<64, KG>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
-                                      &s_free[t], abort_flag);
+                                      abort_flag);
       if (!ok) break;
-      // every lane's P stores are fenced for the async proxy; the warp converges and
-      // one lane arrives for it
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      mbar_arrive(&p_full[t]);
       ++cnt;
       have = nhave;
       j0 = nj0;
