@@ -872,9 +872,12 @@ static inline int64_t k_scale_index(int64_t j, int k_gran) {
     return k_gran == 1 ? (j / 64) * 4 + (j % 8) / 2 : j / 64;
 }
 
-/* 2^x on the FMA pipe, the attention kernel's own polynomial (attn.cu exp2_poly,
+/* 2^x on the FMA pipe, the attention kernel's own polynomial (attn.cu exp2_poly2,
  * fitted for that kernel): j = rint(x) through the 1.5 * 2^23 constant, 2^(x - j)
  * by a degree-3 polynomial, j added to the exponent field; x clamped at -125. */
+#ifndef H3BO_ATTN_POLY_MASK16
+#define H3BO_ATTN_POLY_MASK16 0x08u
+#endif
 static float attn_exp2_poly(float x) {
     const float kM = 12582912.0f;
     const float P0 = 0.9999280571937561f, P1 = 0.6932609677314758f, P2 = 0.2426111251115799f,
@@ -902,7 +905,9 @@ static float attn_exp2(float x) {
  *   tmax  = max over the step's groups of (max_j v_j - 1.5 * 2^23) * c
  *   m     = tmax if tmax > m + 2 else m (lazy running max); alpha = 2^(m_old - m)
  *   x_j   = fma(v_j, c, (log2 112 - m) - 1.5 * 2^23 * c)
- *   P_j   = 2^x_j: the polynomial above on columns 6, 7 of every 16 of a block,
+ *   P_j   = 2^x_j: the polynomial above on the column pairs (2i, 2i + 1) of every 16
+ *           columns of a block whose bit i is set in H3BO_ATTN_POLY_MASK16 (the
+ *           kernel's kPolyMask16),
  *           ex2 (hardware, modelled by a correctly rounded exp2) on the others
  *   l     = l * alpha + (sum of the step's fp32 P_j in the kernel's order)
  *   O     = O * alpha + sum_j E4M3(P_j) * E4M3(V_j) * (accumulated in double here;
@@ -986,7 +991,7 @@ void h3bo_attention_kernel(const int8_t* q, const float* qscale, int q_gran, int
                         for (int cidx = 0; cidx < 64; ++cidx) {
                             const int g = k_gran == 1 ? (cidx % 8) / 2 : 0;
                             const float x = fmaf(v[u][cidx], c[u][g], oo[g]);
-                            const int poly = (cidx % 16) == 6 || (cidx % 16) == 7;
+                            const int poly = (int)((H3BO_ATTN_POLY_MASK16 >> ((cidx % 16) >> 1)) & 1u);
                             p[cidx] = poly ? attn_exp2_poly(x) : attn_exp2(x);
                         }
                         /* the kernel's order: four fp32 accumulators over packed pairs */

@@ -1,10 +1,13 @@
 // attn.cu -- SageAttention-style quantized attention for sm_100a, dense or
 // driven by a Sparge block bitmap.
 //
-//   S = Q_i8 . K_i8^T   tcgen05.mma kind::i8 into tensor memory that was
-//       pre-filled with 0x4B400000: the accumulator then holds the bits of the
-//       float 1.5*2^23 + S (|S| < 2^22), so S needs no integer->float conversion
-//       and the block maximum is an integer maximum of the raw bits
+//   S = Q_i8 . K_i8^T   tcgen05.mma kind::i8 accumulating onto tensor memory
+//       that a bf16 MMA (kind::f16, K = 16, constant operands) has just set to
+//       the float 1.5*2^23 (bits 0x4B400000): the accumulator then holds the
+//       bits of the float 1.5*2^23 + S (|S| < 2^22), so S needs no integer->
+//       float conversion and the block maximum is an integer maximum of the raw
+//       bits; the bias is written by the tensor pipe, in order with the S MMAs,
+//       instead of by the softmax threads
 //   P = exp2(S * qs * ks * scale * log2 e - m) * 112 -> E4M3 (shared memory);
 //       qs per query row group (q_block rows, or Sage per_thread: rows of equal
 //       r % 8 in each 32), ks per 64-key block or per_thread group (keys of equal
@@ -13,7 +16,8 @@
 //       a tile's scores exceed it by more than kTau = 2, so P <= 2^kTau * 112 =
 //       448, the E4M3 maximum, and the O rescale in tensor memory is rare.
 //       Seven columns in eight take ex2.approx (MUFU), the eighth a polynomial
-//       on the FMA pipe (packed fp32 pairs), which balances the two pipes.
+//       on the FMA pipe (packed fp32 pairs), which balances the two pipes
+//       (kPolyMask16 selects the polynomial columns).
 //   O += P . V          tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32, tensor memory)
 //   out = O / l * v_scale[d] -> bf16, l the fp32 row sum of P
 //
@@ -29,13 +33,13 @@
 //   warps 2, 3  MMA issuers of tiles A and B (warp-wide loop over the step
 //               schedule, descriptors in uniform registers, one elected lane
 //               issues): at each of its tile's steps, once the previous P is
-//               written, S(step) and PV(previous step)
+//               written, the bias MMA and S(step), then PV(previous step)
 //               P is double-buffered per tile in shared memory.
 //   warps 4..7  softmax of tile A, warps 8..11 of tile B: one query row per
 //               thread (its TMEM lane): S row from TMEM, per-block dequant
 //               scales, online max / sum, P row to shared memory in the
-//               128-byte-swizzled K-major layout the MMA reads, the S columns
-//               re-biased, O rescaled when the max moves, final normalisation.
+//               128-byte-swizzled K-major layout the MMA reads, O rescaled
+//               when the max moves, final normalisation.
 // Every SM sub-partition thus runs two independent softmax warps (one per
 // tile), and in dense attention each K/V pair is loaded once for 256 queries.
 // TMEM: S_A 0..127, S_B 128..255, O_A 256..383, O_B 384..511.
@@ -62,10 +66,10 @@ constexpr int kOffQ = 0;                          // 2 tiles
 constexpr int kOffP = kOffQ + 2 * kQBytes;        // 2 tiles x 2 buffers
 constexpr int kOffKV = kOffP + 4 * kPBytes;
 constexpr int kOffBar = kOffKV + kKVStages * kKVBytes;
-constexpr int kAttnSmem = kOffBar + 256 + 1024;
+constexpr int kOffBias = kOffBar + 256;          // 8 x 16-byte rows each: A and B of the bias MMA
+constexpr int kAttnSmem = kOffBias + 256 + 1024;
 constexpr float kLog2_112 = 6.807354922057604f;
 constexpr float kTau = 2.0f;
-constexpr uint32_t kMagic = 0x4B400000u;          // bits of 12582912.0f = 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 
 // One query tile's selected K blocks, ascending, taken two at a time.
@@ -161,15 +165,13 @@ __device__ __forceinline__ void ld_early_kg(const float* p, float (&v)[KG]) {
                  : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "l"(p));
   }
 }
+// K-major operand without swizzle whose every 8-row group and both 8-element K halves
+// read the same 8 x 16-byte core matrix (leading and stride byte offsets 0)
+__device__ __forceinline__ uint64_t sdesc_core_repeat(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr & 0x3FFFF) >> 4) | ((uint64_t)1 << 46);
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
 }
 
 // ---------------------------------------------------------------- softmax pieces
@@ -182,16 +184,6 @@ __device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
 // squares on Chebyshev nodes, relative error < 7.5e-5)
 constexpr float kP0 = 0.9999280571937561f, kP1 = 0.6932609677314758f, kP2 = 0.2426111251115799f,
                 kP3 = 0.05517164617776871f;
-// 2^x on the FMA pipe: j = rint(x) by the 1.5 * 2^23 rounding constant (whose
-// low bits then hold j), 2^(x - j) by the polynomial, j added to the exponent
-// field.  x is clamped at -125, so the result stays a normal float (< 2^-124).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + kMagicF;
-  const float f = x - (t - kMagicF);
-  const float p = fmaf(fmaf(fmaf(kP3, f, kP2), f, kP1), f, kP0);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
-}
 // four floats -> four E4M3 bytes (satfinite, round to nearest even), a lowest
 __device__ __forceinline__ uint32_t e4m3x4_f32(float a, float b, float c, float d) {
   uint32_t r;
@@ -258,10 +250,28 @@ __device__ __forceinline__ void raw_max_ragged_g(uint32_t (&s)[128], int n, int 
   }
 }
 
+// Columns whose exponential runs as the polynomial on the FMA pipe (the others take
+// ex2.approx on the MUFU pipe): bit i of kPolyMask16 selects the column pair
+// (2i, 2i + 1) of every 16 columns.  0x08: columns 6, 7 of every 16.
+constexpr uint32_t kPolyMask16 = 0x08u;
+__host__ __device__ constexpr bool poly_pair(int col) { return (kPolyMask16 >> ((col & 15) >> 1)) & 1u; }
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  // 2^x = 2^j * 2^f, j = rint(x) (low bits of t), f = x - j (exact); x clamped at -125
+  const float2 kM = make_float2(kMagicF, kMagicF), kNM = make_float2(-kMagicF, -kMagicF);
+  const float2 kN1 = make_float2(-1.f, -1.f);
+  const float2 q0 = make_float2(kP0, kP0), q1 = make_float2(kP1, kP1), q2 = make_float2(kP2, kP2),
+               q3 = make_float2(kP3, kP3);
+  const float2 xp = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+  const float2 t = __fadd2_rn(xp, kM);
+  const float2 f = __ffma2_rn(__fadd2_rn(t, kNM), kN1, xp);
+  const float2 q = __ffma2_rn(__ffma2_rn(__ffma2_rn(q3, f, q2), f, q1), f, q0);
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // P = 2^(S * cc + oo) over columns [CB, CB + 64), written back as floats, on
-// packed fp32 pairs (FFMA2 / FADD2).  Of every 16 columns, 14 take ex2.approx
-// (MUFU) and 2 the polynomial exponential on the FMA pipe (the split measured
-// fastest against 1 in 4, 1 in 16 and none); returns the sum.
+// packed fp32 pairs (FFMA2 / FADD2); the column pairs poly_pair() selects take the
+// polynomial, the others ex2.approx; returns the sum.
 // KG = 4 (per_thread K scales): pair k of each 8-column chunk is scale group k.
 template <int CB, int KG>
 __device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)[KG], const float (&oo)[KG]) {
@@ -271,10 +281,6 @@ __device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)
     c2[g] = make_float2(cc[g], cc[g]);
     o2[g] = make_float2(oo[g], oo[g]);
   }
-  const float2 kM = make_float2(kMagicF, kMagicF), kNM = make_float2(-kMagicF, -kMagicF);
-  const float2 kN1 = make_float2(-1.f, -1.f);
-  const float2 q0 = make_float2(kP0, kP0), q1 = make_float2(kP1, kP1), q2 = make_float2(kP2, kP2),
-               q3 = make_float2(kP3, kP3);
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < 64; c += 8) {
@@ -284,18 +290,8 @@ __device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)
       x[k] = __ffma2_rn(make_float2(__uint_as_float(s[CB + c + 2 * k]), __uint_as_float(s[CB + c + 2 * k + 1])),
                         c2[KG == 1 ? 0 : k], o2[KG == 1 ? 0 : k]);
 #pragma unroll
-    for (int k = 0; k < 3; ++k) p[k] = make_float2(ex2(x[k].x), ex2(x[k].y));
-    if ((c >> 3) & 1) {
-      p[3] = make_float2(ex2(x[3].x), ex2(x[3].y));
-    } else {
-      // 2^x = 2^j * 2^f, j = rint(x) (low bits of t), f = x - j (exact)
-      const float2 xp = make_float2(fmaxf(x[3].x, -125.0f), fmaxf(x[3].y, -125.0f));
-      const float2 t = __fadd2_rn(xp, kM);
-      const float2 f = __ffma2_rn(__fadd2_rn(t, kNM), kN1, xp);
-      const float2 q = __ffma2_rn(__ffma2_rn(__ffma2_rn(q3, f, q2), f, q1), f, q0);
-      p[3] = make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
-                         __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
-    }
+    for (int k = 0; k < 4; ++k)
+      p[k] = poly_pair(c + 2 * k) ? exp2_poly2(x[k]) : make_float2(ex2(x[k].x), ex2(x[k].y));
     acc0 = __fadd2_rn(acc0, p[0]);
     acc1 = __fadd2_rn(acc1, p[1]);
     acc0 = __fadd2_rn(acc0, p[2]);
@@ -325,17 +321,6 @@ __device__ __forceinline__ void store_p(const uint32_t (&s)[128], uint8_t* prow,
     *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = w;
   }
 }
-template <int NC>
-__device__ __forceinline__ void rebias_s(uint32_t s_addr) {
-  __syncwarp();
-  tmem_st32_const(s_addr, kMagic);
-  tmem_st32_const(s_addr + 32, kMagic);
-  if constexpr (NC == 128) {
-    tmem_st32_const(s_addr + 64, kMagic);
-    tmem_st32_const(s_addr + 96, kMagic);
-  }
-}
-
 // One key pair (or a single trailing block, NC = 64) for one query row of one
 // tile.  The second block's scores load from TMEM while the first block's
 // maximum is taken.  The running max m moves (to the tile max) only when the
@@ -409,7 +394,6 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
       }
     }
   }
-  rebias_s<NC>(s_addr);
   const float off = kLog2_112 - m;
   float o0[KG];
 #pragma unroll
@@ -467,6 +451,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(&o_full[0], 1);
     mbar_init(&o_full[1], 1);
     *abort_flag = 0;
+    // bias operands: A = 1.0 and B = 0.75 * 2^23 in element 0 of each core row (bf16),
+    // so A . B^T over K = 16 (two copies of the core row) is 1.5 * 2^23 everywhere
+    uint32_t* bias = reinterpret_cast<uint32_t*>(smem + kOffBias);
+    for (int i = 0; i < 64; ++i) bias[i] = (i & 3) == 0 ? ((i < 32) ? 0x3F80u : 0x4AC0u) : 0u;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -482,15 +470,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp >= 4) {
-    // bias both S accumulators: every S MMA accumulates onto 1.5 * 2^23
-    const int t = (warp - 4) >> 2;
-    const uint32_t sa = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(t * 128);
-    __syncwarp();
-#pragma unroll
-    for (int c = 0; c < 128; c += 32) tmem_st32_const(sa + c, kMagic);
-    tmem_wait_st();
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -545,6 +524,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ + t * kQBytes));
     const uint32_t pbase0 = smem_u32(smem + kOffP + 2 * t * kPBytes);  // P buffer of this tile's even steps
     const uint32_t kv_addr = smem_u32(smem + kOffKV);
+    const uint64_t bias_a = sdesc_core_repeat(smem_u32(smem + kOffBias));
+    const uint64_t bias_b = sdesc_core_repeat(smem_u32(smem + kOffBias + 128));
     const uint32_t s_tmem = tmem + (uint32_t)(t * 128);
     const uint32_t o_tmem = tmem + 256 + (uint32_t)(t * 128);
     int stage = 0;
@@ -588,6 +569,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint64_t kdesc = sdesc_kmajor_sw128(kv_addr + (uint32_t)(stage * kKVBytes));
         const uint32_t idesc_s = two ? idesc_i8(128, 128) : idesc_i8(128, 64);
         if (elect_one()) {
+          mma_bf16_ss(s_tmem, bias_a, bias_b, two ? idesc_bf16(128, 128) : idesc_bf16(128, 64), 0u);
 #pragma unroll
           for (int k = 0; k < 4; ++k) mma_i8_ss(s_tmem, qdesc + (uint64_t)(2 * k), kdesc + (uint64_t)(2 * k), idesc_s, 1u);
           mma_commit(&s_full[t]);
