@@ -198,6 +198,14 @@ int h3b_w4a8_group_sums(const void* xq, const void* xs, int64_t M, int64_t K, in
 int h3b_bf16_gemm_accumulate(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
                              int64_t out_row_stride, void* stream);
 
+/* The block's AdaLN projection: out[r, n] = bf16(sum_k t[r, k] * w[n, k] + b[n]) with
+ * fp32 products and sums, for 1..8 rows of t.  w: bf16 [N, K] row-major, t: bf16
+ * [rows, K], b: bf16 [N] or NULL, out: bf16 [rows, N]; K a multiple of 8, w and t
+ * 16-byte aligned.  Replaces the engine's adaln_projector linear over the timestep
+ * rows (model/layers.py:1083-1085; the base linear of model/lora.py:524-570). */
+int h3b_adaln_projection(const void* w, const void* t, const void* b, int64_t rows, int64_t N, int64_t K,
+                         void* out, void* stream);
+
 /* ---------------------------------------------------------------- attention preparation */
 
 /* Bytes of workspace h3b_key_mean needs for L tokens and H heads. */

@@ -62,6 +62,9 @@ def test_unsupported_shapes_are_rejected():
     assert lib().h3b_selftest_bounded_wait(0, None) == -1
     assert lib().h3b_selftest_bounded_wait(2_000_000_000, None) == -1
     assert lib().h3b_bf16_gemm_accumulate(dummy, dummy, dummy, 8, 8, 12, 8, None) == -2
+    assert lib().h3b_adaln_projection(dummy, dummy, None, 9, 64, 64, dummy, None) == -2    # 1..8 rows
+    assert lib().h3b_adaln_projection(dummy, dummy, None, 1, 64, 12, dummy, None) == -1    # K % 8
+    assert lib().h3b_adaln_projection(dummy, ctypes.c_void_p(24), None, 1, 64, 64, dummy, None) == -2
 
 
 def test_qkv_qk_rope_entry_rejects_what_it_does_not_take():

@@ -269,8 +269,8 @@ def test_linear_vs_reference_outputs(ops):
     assert rel_l2(w4.float(), from_bits(z["out_w4_module"]).float()) < 2e-2
 
 
-def test_module_injection_matches_reference_module(ops):
-    """h3b_int8_kernel injected into the engine's Int8Kernel slot reproduces the
+def test_int8_kernel_callable_matches_oracle(ops):
+    """h3b_int8_kernel, the callable the engine's Int8Kernel slot takes, reproduces the
     oracle bit for bit (same quant + GEMM + epilogue)."""
     from h3b import h3b_int8_kernel
     z = np.load(os.path.join(G, "linear.npz"))
@@ -279,6 +279,25 @@ def test_module_injection_matches_reference_module(ops):
                           from_bits(z["bias"]), 256)
     ref = O.int8_linear(z["x"], z["wq"], z["ws"], O.bf16_bits_to_f32(z["bias"]), convrot=256)
     np.testing.assert_array_equal(bits(out), ref)
+
+
+@pytest.mark.parametrize("rows,n,k", [(1, 24576, 4096), (3, 18 * 256, 8), (8, 1000, 264), (5, 96, 4096)])
+def test_adaln_projection(ops, rows, n, k):
+    """The AdaLN projection GEMV against torch's fp32 product of the same bf16 operands:
+    the fp32 sums differ only in order, so after bf16 rounding at most one bf16 ulp
+    apart, and nearly all equal."""
+    g = torch.Generator().manual_seed(rows * 7 + k)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    t = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    out = ops.adaln_projection(w.cuda(), b.cuda(), t.cuda())
+    ref = (t.double() @ w.double().T + b.double()).float().to(torch.bfloat16)
+    ulps = _bf16_ulps(bits(out), bits(ref))
+    assert ulps.max() <= 1
+    assert (ulps == 0).mean() > 0.98
+    one = ops.adaln_projection(w.cuda(), None, t[0].cuda())
+    ref1 = (t[:1].double() @ w.double().T).float().to(torch.bfloat16)
+    assert _bf16_ulps(bits(one), bits(ref1)).max() <= 1
 
 
 def test_no_device_timeouts_recorded(ops):

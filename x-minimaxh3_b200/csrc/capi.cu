@@ -291,6 +291,20 @@ int h3b_w4a8_group_sums(const void* xq, const void* xs, int64_t M, int64_t K, in
                      "w4a8_group_sums");
 }
 
+int h3b_adaln_projection(const void* w, const void* t, const void* b, int64_t rows, int64_t N, int64_t K,
+                         void* out, void* stream) {
+  if (N == 0) return ok();
+  if (!w || !t || !out) return fail(H3B_ERR_INVALID_ARGUMENT, "null pointer");
+  if (rows < 1 || rows > 8) return fail(H3B_ERR_UNSUPPORTED, "adaln_projection: 1..8 rows of t");
+  if (N < 0 || K <= 0 || K % 8) return fail(H3B_ERR_INVALID_ARGUMENT, "adaln_projection: K must be a positive multiple of 8");
+  if (!aligned16(w) || !aligned16(t)) return fail(H3B_ERR_UNSUPPORTED, "w and t must be 16-byte aligned");
+  if (N > (int64_t)INT_MAX * 8) return fail(H3B_ERR_UNSUPPORTED, "adaln_projection: N too large");
+  return cuda_status(h3b::launch_adaln_projection(static_cast<const uint16_t*>(w), static_cast<const uint16_t*>(t),
+                                                  static_cast<const uint16_t*>(b), rows, N, K,
+                                                  static_cast<uint16_t*>(out), st(stream)),
+                     "adaln_projection");
+}
+
 int h3b_bf16_gemm_accumulate(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
                              int64_t out_row_stride, void* stream) {
   if (M == 0 || N == 0) return ok();

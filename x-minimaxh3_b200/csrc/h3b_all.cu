@@ -7,4 +7,5 @@
 #include "attn_mask.cu"
 #include "attn.cu"
 #include "ulysses.cu"
+#include "adaln.cu"
 #include "capi.cu"

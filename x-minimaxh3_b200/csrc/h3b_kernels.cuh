@@ -69,6 +69,8 @@ bool make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int 
 
 // sx[m, g] = bf16(bf16(sum of xq[m, g*G .. g*G+G-1]) * bf16(xs[m])) for g < K/G, columns
 // [K/G, sx_stride) zero: the W4A8 group-correction activations
+cudaError_t launch_adaln_projection(const uint16_t* w, const uint16_t* t, const uint16_t* b, int64_t rows,
+                                    int64_t n, int64_t k, uint16_t* out, cudaStream_t s);
 cudaError_t launch_group_sums(const int8_t* xq, const float* xs, int64_t M, int64_t K, int64_t G, uint16_t* sx,
                               int64_t sx_stride, cudaStream_t s);
 cudaError_t launch_w4_decode(const void* qw, const void* s_rel, int s_rel_kind, const void* codebook, void* out,

@@ -67,6 +67,7 @@ _SIGNATURES = {
                                          c_void_p],
     "h3b_w4a8_group_sums": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p],
     "h3b_bf16_gemm_accumulate": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "h3b_adaln_projection": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "h3b_key_mean_workspace_bytes": [c_int64, c_int64],
     "h3b_key_mean": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
     "h3b_key_mean_no_alloc": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],

@@ -1,7 +1,7 @@
 """An H3-shaped DiT block on the B200 kernels (the benchmark's unit of work).
 
 Per block (model/layers.py:1074-1298, fused_mlp.py:269-426):
-  adaln(t) -> shift/scale/gate x 2           (torch matmul; one GEMV per step)
+  adaln(t) -> shift/scale/gate x 2           h3b_adaln_projection (one GEMV per step)
   xq = rms_adaln + ConvRot + INT8(x)          h3b_rms_adaln_quantize_int8
   qkv = INT8 GEMM(xq, W_qkv) + bias, with    h3b_int8_gemm_dequant_qk_rope (one kernel;
     q, k <- per-head RMSNorm + 3-D RoPE       h3b_int8_gemm_dequant + h3b_qk_rmsnorm_rope
@@ -186,7 +186,8 @@ class DiTBlockB200:
         """A block over given weights (bf16 vectors / AdaLN projection, quantization layers)."""
         blk = cls.__new__(cls)
         blk._setup(cfg, device, group)
-        blk.ada_w, blk.ada_b = ada_w, ada_b
+        blk.ada_w = ada_w.to(torch.bfloat16).contiguous()
+        blk.ada_b = None if ada_b is None else ada_b.to(torch.bfloat16).contiguous()
         blk.norm1, blk.norm2, blk.q_norm, blk.k_norm = norm1, norm2, q_norm, k_norm
         blk.qkv, blk.out, blk.fc1, blk.fc2 = qkv, out, fc1, fc2
         W = cfg.heads * cfg.head_dim
@@ -208,10 +209,8 @@ class DiTBlockB200:
         from the projection input t [t_dim] or [rows, t_dim].  A projection to 18 * hidden
         (the H3 checkpoints) gives three modulation rows per input row, selected by
         `segments` (model/layers.py:910-913)."""
-        w, b = self.ada_w.float(), self.ada_b.float()
-        tf = t.to(self.device).float()
-        out = torch.mv(w, tf.reshape(-1)) + b if tf.dim() == 1 or tf.shape[0] == 1 else tf @ w.T + b
-        return out.reshape(-1, 6, self.cfg.hidden).to(torch.bfloat16)
+        out = ops.adaln_projection(self.ada_w, self.ada_b, t.to(self.device))
+        return out.reshape(-1, 6, self.cfg.hidden)
 
     def attention(self, qkv_heads: torch.Tensor) -> torch.Tensor:
         """qkv_heads: [L, 3*h*128] -> o [L, h, 128] (h heads of this rank)."""

@@ -445,3 +445,29 @@ def w4a8_group_correction_(out: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor
     check(lib().h3b_bf16_gemm_accumulate(_p(sx), _p(op), _p(out2), M, N, kp, out2.stride(0), _stream(xq)),
           "bf16_gemm_accumulate")
     return out
+
+
+# ----------------------------------------------------------------------------- AdaLN projection
+
+
+def adaln_projection(weight: torch.Tensor, bias: torch.Tensor | None, t: torch.Tensor) -> torch.Tensor:
+    """bf16 [R, N] = bf16(t @ weight^T + bias) with fp32 products and sums on the GPU, for
+    t [K] or [R, K] (rounded to bf16 first, as the engine's bf16 projector linear sees
+    it) and a bf16 weight [N, K] (the engine's adaln_projector, model/layers.py:1083-1085)."""
+    _cuda("adaln_projection", weight, t)
+    if weight.dtype != torch.bfloat16 or weight.ndim != 2:
+        raise ValueError("the AdaLN projection weight must be a bfloat16 matrix [N, K]")
+    N, K = weight.shape
+    t2 = t.reshape(-1, K).to(torch.bfloat16).contiguous()
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    b = None
+    if bias is not None:
+        b = bias.to(torch.bfloat16).reshape(-1).contiguous()
+        if b.numel() != N:
+            raise ValueError("bias does not match the projection's output width")
+    out = torch.empty((t2.shape[0], N), device=weight.device, dtype=torch.bfloat16)
+    for r0 in range(0, t2.shape[0], 8):
+        rows = min(8, t2.shape[0] - r0)
+        check(lib().h3b_adaln_projection(_p(w), _p(t2[r0:r0 + rows]), _p(b), rows, N, K, _p(out[r0:r0 + rows]),
+                                         _stream(w)), "adaln_projection")
+    return out
