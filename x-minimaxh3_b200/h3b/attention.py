@@ -75,13 +75,22 @@ class PreparedValues:
     padded: int
 
 
+_THRESHOLDS: dict[tuple, torch.Tensor] = {}
+
+
 def _thr(threshold, H: int, device) -> torch.Tensor:
     if isinstance(threshold, torch.Tensor):
         t = threshold.to(device=device, dtype=torch.float32).reshape(-1)
         if t.numel() == 1:
             t = t.expand(H)
         return t.contiguous()
-    return torch.full((H,), float(threshold), device=device, dtype=torch.float32)
+    # a scalar threshold: its [H] device copy is made once per (value, H, device)
+    key = (float(threshold), H, str(device))
+    t = _THRESHOLDS.get(key)
+    if t is None:
+        t = torch.full((H,), float(threshold), device=device, dtype=torch.float32)
+        _THRESHOLDS[key] = t
+    return t
 
 
 def key_mean(k: torch.Tensor, workspace: torch.Tensor | None = None) -> torch.Tensor:

@@ -121,6 +121,18 @@ class _QuantLinear:
     bias: torch.Tensor | None
 
     @property
+    def bias_f32(self) -> torch.Tensor | None:
+        """The bias as the fp32 vector the GEMM epilogues read, converted once."""
+        b = self.bias
+        if b is None:
+            return None
+        cached = getattr(self, "_bias_f32", None)
+        if cached is None or cached[0] is not b:
+            cached = (b, b.to(torch.float32).reshape(-1).contiguous())
+            self._bias_f32 = cached
+        return cached[1]
+
+    @property
     def convrot_group_size(self) -> int:
         """ConvRot group of the activation quantizer, 0 for a plain row quantizer."""
         return CONVROT_GROUP if self.spec_convrot else 0
@@ -136,7 +148,7 @@ class _QuantLinear:
     def forward_prequantized(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """bf16 [M, N] from quantized rows; `out` (bf16 rows with unit column stride) receives it when given."""
         w8, ws = self.int8_weight()
-        out = ops.int8_linear_prequantized(xq, xs, w8, ws, self.bias, out=out)
+        out = ops.int8_linear_prequantized(xq, xs, w8, ws, self.bias_f32, out=out)
         self._correct_(out, xq, xs)
         return out
 
@@ -150,7 +162,7 @@ class _QuantLinear:
         if (input_act == "gelu_tanh" and next_layer.spec_convrot
                 and getattr(self, "correction", None) is None):
             w8, ws = self.int8_weight()
-            return ops.int8_linear_gelu_convrot_quantize(xq, xs, w8, ws, self.bias)
+            return ops.int8_linear_gelu_convrot_quantize(xq, xs, w8, ws, self.bias_f32)
         h = self.forward_prequantized(xq, xs)
         return next_layer.quantize(h, input_act)
 
@@ -162,7 +174,7 @@ class _QuantLinear:
         post-GEMM correction; the same values either way."""
         if getattr(self, "correction", None) is None:
             w8, ws = self.int8_weight()
-            return ops.int8_linear_prequantized_qk_rope(xq, xs, w8, ws, self.bias, out, heads, q_offset, k_offset,
+            return ops.int8_linear_prequantized_qk_rope(xq, xs, w8, ws, self.bias_f32, out, heads, q_offset, k_offset,
                                                         q_weight, k_weight, cos_table, sin_table, eps)
         self.forward_prequantized(xq, xs, out=out)
         return ops.qk_rmsnorm_rope_(out, heads, q_offset, k_offset, q_weight, k_weight, cos_table, sin_table, eps)
@@ -172,7 +184,7 @@ class _QuantLinear:
         """residual += bf16(layer(x)) * gate with one bf16 rounding (model/layers.py:944-960)."""
         if getattr(self, "correction", None) is None:
             w8, ws = self.int8_weight()
-            return ops.int8_linear_gated_residual_(residual, gate, xq, xs, w8, ws, self.bias)
+            return ops.int8_linear_gated_residual_(residual, gate, xq, xs, w8, ws, self.bias_f32)
         update = self.forward_prequantized(xq, xs)
         return residual.addcmul_(update, gate.to(update.dtype))
 
