@@ -219,12 +219,31 @@ class DiTBlockB200:
         h = qkv_heads.shape[1] // (3 * cfg.head_dim)
         view = qkv_heads.view(L, 3, h, cfg.head_dim)
         q, k, v = view[:, 0], view[:, 1], view[:, 2]
-        pv = A.prepare_values(v)
+        # the three preparations are independent and none fills the GPU alone: V and Q
+        # run on side streams while K (mean, pooling, INT8) runs on the current stream
+        main = torch.cuda.current_stream(self.device)
+        side = self._side_streams()
+        for st in side:
+            st.wait_stream(main)
+        with torch.cuda.stream(side[0]):
+            pv = A.prepare_values(v)
+        with torch.cuda.stream(side[1]):
+            pq = A.prepare_queries(q)
         pk, _ = A.prepare_keys(k)
-        pq = A.prepare_queries(q)
+        main.wait_stream(side[1])
+        _used_on(main, pq.pooled, pq.similar, pq.qi8, pq.scale)
         bitmap = A.block_mask(pq, pk, cfg.mask) if cfg.mask is not None else None
+        main.wait_stream(side[0])
+        _used_on(main, pv.vt, pv.scale)
         self._last_attn = (pq, pk, pv, bitmap)
         return A.attention(pq, pk, pv, bitmap)
+
+    def _side_streams(self) -> tuple[torch.cuda.Stream, torch.cuda.Stream]:
+        streams = getattr(self, "_streams", None)
+        if streams is None:
+            streams = (torch.cuda.Stream(device=self.device), torch.cuda.Stream(device=self.device))
+            self._streams = streams
+        return streams
 
     def attention_ulysses(self, qkv: torch.Tensor) -> torch.Tensor:
         """qkv: this rank's token rows [L/P, 3*H*128] -> o [L, H/P, 128] for this rank's
@@ -428,6 +447,14 @@ class HostPipeline:
             else:
                 read_out[b] = store(k, 0, whole[1])
         comp.wait_stream(self.s_out)
+
+
+def _used_on(stream: torch.cuda.Stream, *tensors: torch.Tensor | None) -> None:
+    """Tensors made on a side stream and consumed on `stream`: their memory is not
+    reused before `stream`'s work up to this point is done."""
+    for t in tensors:
+        if t is not None:
+            t.record_stream(stream)
 
 
 def kept_tiles_per_head(bitmap: torch.Tensor) -> torch.Tensor:
