@@ -135,6 +135,7 @@ KERNEL_CASES = """
     w4_decode                  h3b_dequant_int4_grouped_to_int8, 16,384 x 4,096, G = 128
     gemm_gelu                  h3b_int8_gemm_gelu_convrot (GELU + ConvRot epilogue), 16,384 x 16,384 x 4,096
     quant_rotated              h3b_quantize_rotated_int8 on its output, 16,384 x 16,384
+    adaln                      h3b_adaln_projection, weight 24,576 x 4,096 (6 x hidden), one timestep row
 """
 
 
@@ -218,6 +219,11 @@ def _kernel_case(name: str, g):
             return fused
         fused()
         return lambda: ops.quantize_rotated_int8(rot, amax)
+    if name == "adaln":
+        w = (torch.randn(6 * 4096, 4096, device=dev, generator=g) * 0.02).bfloat16()
+        b = (torch.randn(6 * 4096, device=dev, generator=g) * 0.02).bfloat16()
+        t = torch.randn(4096, device=dev, generator=g).bfloat16()
+        return lambda: ops.adaln_projection(w, b, t)
     raise SystemExit(f"unknown case {name!r}; cases:{KERNEL_CASES}")
 
 
