@@ -80,6 +80,11 @@ def test_config2_w4a8_mlp_full_size(h3b_mods):
     xq, xs = fc1.quantize(x)
     h = fc1.forward_prequantized(xq, xs)
     hq, hs = fc2.quantize(h, "gelu_tanh")
+    # the block's path: tanh-GELU + ConvRot in FC1's GEMM epilogue, then the codes pass;
+    # every row's codes and scale equal the unfused FC1 + GELU quantizer's
+    hq_f, hs_f = fc1.forward_prequantized_for(fc2, xq, xs, "gelu_tanh")
+    assert torch.equal(hq_f, hq) and torch.equal(hs_f.reshape(-1), hs.reshape(-1))
+    del hq_f, hs_f
     res = res0.clone()
     fc2.gated_residual_(res, gate.cuda(), hq, hs)
     torch.cuda.synchronize()
