@@ -360,7 +360,7 @@ class HostPipeline:
     chunk by chunk there).  All ordering is by CUDA events; nothing waits on the host.
     """
 
-    def __init__(self, block: DiTBlockB200, rope: tuple[torch.Tensor, torch.Tensor], tokens: int, chunks: int = 4):
+    def __init__(self, block: DiTBlockB200, rope: tuple[torch.Tensor, torch.Tensor], tokens: int, chunks: int = 8):
         dev = block.device
         self.block, self.rope = block, rope
         self.x = [torch.empty((tokens, block.cfg.hidden), device=dev, dtype=torch.bfloat16) for _ in range(2)]
