@@ -34,6 +34,21 @@ __device__ __forceinline__ float2 bf16r2(float2 v) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v.y), "f"(v.x));
   return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
 }
+// both lanes rounded to bf16 and packed (lane x in bits 0..15, lane y in 16..31)
+__device__ __forceinline__ uint32_t pack_bf16x2(float2 v) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v.y), "f"(v.x));
+  return p;
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t p) {
+  return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
+}
+// packed bf16 sum, correctly rounded (add.rn.bf16x2)
+__device__ __forceinline__ uint32_t hadd2_bf16(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 __device__ __forceinline__ float2 div2_rn_by(float2 a, float2 b, float2 rb) {
   const float2 q = mul2(a, rb);
   const float2 r = fma2(q, make_float2(-b.x, -b.y), a);

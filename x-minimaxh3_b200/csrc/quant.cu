@@ -178,7 +178,8 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t ro
       const uint16_t* tabs[3] = {a.norm_w, a.scale_tab + (int64_t)r * K, a.shift_tab + (int64_t)r * K};
 #pragma unroll
       for (int h = 0; h < 2; ++h) {  // 8 columns of each lane at a time
-        float2 w[3][8];
+        // the tables as bf16 pairs (lane x column, lane y column): pair j is column 8h + j
+        uint32_t w[3][8];
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
           const uint4 z = make_uint4(0u, 0u, 0u, 0u);
@@ -187,15 +188,20 @@ __global__ void __launch_bounds__(512) quant_rows_kernel(QuantArgs a, int64_t ro
           const uint32_t qx[4] = {wx.x, wx.y, wx.z, wx.w}, qy[4] = {wy.x, wy.y, wy.z, wy.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            w[k][2 * i] = make_float2(__uint_as_float(qx[i] << 16), __uint_as_float(qy[i] << 16));
-            w[k][2 * i + 1] = make_float2(__uint_as_float(qx[i] & 0xffff0000u), __uint_as_float(qy[i] & 0xffff0000u));
+            w[k][2 * i] = __byte_perm(qx[i], qy[i], 0x5410);
+            w[k][2 * i + 1] = __byte_perm(qx[i], qy[i], 0x7632);
           }
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float2 n = bf16r2(mul2(mul2(v[8 * h + j], inv), w[0][j]));
-          n = bf16r2(mul2(n, bf16r2(add2(splat2(1.0f), w[1][j]))));
-          v[8 * h + j] = bf16r2(add2(n, w[2][j]));
+          // bf16(x * inv * w); bf16(n * bf16(1 + scale)) with an fp32 product; bf16(n + shift).
+          // The two adds of bf16 operands are packed bf16 adds: for bf16 operands the
+          // correctly rounded bf16 sum equals the fp32 sum rounded to bf16 (the fp32 sum is
+          // exact unless the exponents differ by more than 16, and then the smaller operand
+          // is below half a bf16 step of the larger)
+          const float2 n = unpack_bf16x2(pack_bf16x2(mul2(mul2(v[8 * h + j], inv), unpack_bf16x2(w[0][j]))));
+          const float2 s1 = unpack_bf16x2(hadd2_bf16(0x3F803F80u, w[1][j]));
+          v[8 * h + j] = unpack_bf16x2(hadd2_bf16(pack_bf16x2(mul2(n, s1)), w[2][j]));
         }
       }
       // dead lanes: weight, scale and shift load as 0, so v stays 0
