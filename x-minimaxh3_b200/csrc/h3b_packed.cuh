@@ -136,6 +136,15 @@ __device__ __forceinline__ float2 gelu_tanh2(float2 v) {
   return mul2(mul2(splat2(0.5f), v), add2(splat2(1.0f), t));
 }
 
+// int8 codes of a pair of values that are already bf16 (bf16(v) = v): code_byte(bf16(v / st))
+// on both lanes, the two code bytes in bits 0..7 (lane x) and 8..15 (lane y); the bits
+// above are not zero (the caller combines two pairs with byte_perm)
+__device__ __forceinline__ uint32_t codes2_bf16(float2 v, float2 st2, float2 rst2) {
+  const float2 d = bf16r2(div2_rn_by(v, st2, rst2));
+  const float2 c = make_float2(fminf(127.0f, fmaxf(-128.0f, d.x)), fminf(127.0f, fmaxf(-128.0f, d.y)));
+  const float2 r = add2(c, splat2(12582912.0f));
+  return __byte_perm(__float_as_uint(r.x), __float_as_uint(r.y), 0x0040u);
+}
 // int8 codes of both lanes: the scalar code_byte(bf16(bf16(v) / st)) lane by lane
 __device__ __forceinline__ void codes2(float2 v, float2 st2, float2 rst2, uint32_t& bx, uint32_t& by) {
   const float2 d = bf16r2(div2_rn_by(bf16r2(v), st2, rst2));

@@ -302,16 +302,14 @@ __global__ void __launch_bounds__(kRotThreads) quant_rotated_kernel(const uint16
       const int c = t + i * kRotThreads;
       if (c >= chunks) continue;
       const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
-      uint32_t lo = 0, hi = 0;
+      uint32_t pr[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t b0, b1;
-        codes2(make_float2(__uint_as_float(ww[j] << 16), __uint_as_float(ww[j] & 0xffff0000u)), st2, rst2, b0, b1);
-        const uint32_t pair = b0 | (b1 << 8);
-        if (j < 2) lo |= pair << (16 * j);
-        else hi |= pair << (16 * (j - 2));
-      }
-      *reinterpret_cast<uint2*>(dst + c * 8) = make_uint2(lo, hi);
+      for (int j = 0; j < 4; ++j)
+        pr[j] = codes2_bf16(make_float2(__uint_as_float(ww[j] << 16), __uint_as_float(ww[j] & 0xffff0000u)), st2,
+                            rst2);
+      // code bytes 0..1 of pairs (0, 1) and (2, 3)
+      *reinterpret_cast<uint2*>(dst + c * 8) =
+          make_uint2(__byte_perm(pr[0], pr[1], 0x5410u), __byte_perm(pr[2], pr[3], 0x5410u));
     }
   }
 }
