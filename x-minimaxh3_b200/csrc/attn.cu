@@ -8,7 +8,8 @@
 //       float conversion and the block maximum is an integer maximum of the raw
 //       bits; the bias is written by the tensor pipe, in order with the S MMAs,
 //       instead of by the softmax threads
-//   P = exp2(S * qs * ks * scale * log2 e - m) * 112 -> E4M3 (shared memory);
+//   P = exp2(S * qs * ks * scale * log2 e - m) * 112 -> E4M3 (tensor memory,
+//       over the S columns the softmax has already read into registers);
 //       qs per query row group (q_block rows, or Sage per_thread: rows of equal
 //       r % 8 in each 32), ks per 64-key block or per_thread group (keys of equal
 //       (j % 8) / 2 in each 64-key block: KG = 4);
@@ -18,14 +19,15 @@
 //       Seven columns in eight take ex2.approx (MUFU), the eighth a polynomial
 //       on the FMA pipe (packed fp32 pairs), which balances the two pipes
 //       (kPolyMask16 selects the polynomial columns).
-//   O += P . V          tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32, tensor memory)
+//   O += P . V          tcgen05.mma kind::f8f6f4, A = P from tensor memory, B = V^T
+//                       from shared memory (E4M3 x E4M3 -> fp32, tensor memory)
 //   out = O / l * v_scale[d] -> bf16, l the fp32 row sum of P
 //
 // One CTA per (two 128-query tiles A and B, head), 384 threads:
 //   warp 0      TMA producer (the warp runs the schedule, one elected lane
 //               issues the copies): both Q tiles once, then one step per PAIR of
 //               selected 64-key blocks (K: 2 x [64 x 128 B], 128-byte swizzle;
-//               V^T: 2 x [128 x 64 B], 64-byte swizzle) into a 4-stage ring; no
+//               V^T: 2 x [128 x 64 B], 64-byte swizzle) into a 6-stage ring; no
 //               multicast.  The steps interleave the two tiles' own block
 //               lists (A, B, A, B, ...); a step whose pair both tiles selected
 //               next (every step of dense attention) serves both tiles
@@ -33,16 +35,19 @@
 //   warps 2, 3  MMA issuers of tiles A and B (warp-wide loop over the step
 //               schedule, descriptors in uniform registers, one elected lane
 //               issues): at each of its tile's steps, once the previous P is
-//               written, the bias MMA and S(step), then PV(previous step)
-//               P is double-buffered per tile in shared memory.
+//               written, PV(previous step), then the bias MMA and S(step); the
+//               MMAs of one thread run in issue order, so the PV has read P
+//               before the next S overwrites its columns
+//               (P needs no shared memory, which leaves room for six K/V stages)
 //   warps 4..7  softmax of tile A, warps 8..11 of tile B: one query row per
 //               thread (its TMEM lane): S row from TMEM, per-block dequant
-//               scales, online max / sum, P row to shared memory in the
-//               128-byte-swizzled K-major layout the MMA reads, O rescaled
+//               scales, online max / sum, P row to tensor memory (S columns
+//               96..127 of its lane: the A operand of the P.V MMA), O rescaled
 //               when the max moves, final normalisation.
 // Every SM sub-partition thus runs two independent softmax warps (one per
 // tile), and in dense attention each K/V pair is loaded once for 256 queries.
-// TMEM: S_A 0..127, S_B 128..255, O_A 256..383, O_B 384..511.
+// TMEM: S_A 0..127, S_B 128..255, O_A 256..383, O_B 384..511; P_A and P_B in
+// columns 96..127 of S_A and S_B.
 #include "h3b_kernels.cuh"
 
 namespace h3b {
@@ -58,13 +63,11 @@ constexpr int kCtrlRegs = 72;
 constexpr int kSoftmaxRegs = 216;
 static_assert(128 * (kCtrlRegs + 2 * kSoftmaxRegs) <= kAttnThreads * kLaunchRegs, "register split too large");
 constexpr int kTileThreads = 128;
-constexpr int kKVStages = 4;
+constexpr int kKVStages = 6;
 constexpr int kQBytes = 128 * 128;
-constexpr int kPBytes = 128 * 128;
 constexpr int kKVBytes = 32768;  // K pair 16 KB + V^T pair 2 x 8 KB
 constexpr int kOffQ = 0;                          // 2 tiles
-constexpr int kOffP = kOffQ + 2 * kQBytes;        // 2 tiles x 2 buffers
-constexpr int kOffKV = kOffP + 4 * kPBytes;
+constexpr int kOffKV = kOffQ + 2 * kQBytes;
 constexpr int kOffBar = kOffKV + kKVStages * kKVBytes;
 constexpr int kOffBias = kOffBar + 256;          // 8 x 16-byte rows each: A and B of the bias MMA
 constexpr int kAttnSmem = kOffBias + 256 + 1024;
@@ -169,9 +172,6 @@ __device__ __forceinline__ void ld_early_kg(const float* p, float (&v)[KG]) {
 // read the same 8 x 16-byte core matrix (leading and stride byte offsets 0)
 __device__ __forceinline__ uint64_t sdesc_core_repeat(uint32_t smem_addr) {
   return (uint64_t)((smem_addr & 0x3FFFF) >> 4) | ((uint64_t)1 << 46);
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- softmax pieces
@@ -305,34 +305,32 @@ __device__ __forceinline__ float exp_block(uint32_t (&s)[128], const float (&cc)
   const float2 t = __fadd2_rn(acc0, acc1);
   return t.x + t.y;
 }
-// P row -> shared memory, K-major, 128-byte swizzle (16-byte chunk c at c ^ (r & 7))
+// P row -> tensor memory: the thread's lane, keys 4c..4c+3 in column c (E4M3, the
+// lowest key in bits 0..7), the A-operand layout of the P.V MMA
 template <int NC>
-__device__ __forceinline__ void store_p(const uint32_t (&s)[128], uint8_t* prow, int r) {
+__device__ __forceinline__ void store_p(const uint32_t (&s)[128], uint32_t p_addr) {
+  uint32_t w[32];
 #pragma unroll
-  for (int c = 0; c < NC / 16; ++c) {
-    const uint4 w = make_uint4(e4m3x4_f32(__uint_as_float(s[16 * c]), __uint_as_float(s[16 * c + 1]),
-                                          __uint_as_float(s[16 * c + 2]), __uint_as_float(s[16 * c + 3])),
-                               e4m3x4_f32(__uint_as_float(s[16 * c + 4]), __uint_as_float(s[16 * c + 5]),
-                                          __uint_as_float(s[16 * c + 6]), __uint_as_float(s[16 * c + 7])),
-                               e4m3x4_f32(__uint_as_float(s[16 * c + 8]), __uint_as_float(s[16 * c + 9]),
-                                          __uint_as_float(s[16 * c + 10]), __uint_as_float(s[16 * c + 11])),
-                               e4m3x4_f32(__uint_as_float(s[16 * c + 12]), __uint_as_float(s[16 * c + 13]),
-                                          __uint_as_float(s[16 * c + 14]), __uint_as_float(s[16 * c + 15])));
-    *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = w;
-  }
+  for (int c = 0; c < NC / 4; ++c)
+    w[c] = e4m3x4_f32(__uint_as_float(s[4 * c]), __uint_as_float(s[4 * c + 1]), __uint_as_float(s[4 * c + 2]),
+                      __uint_as_float(s[4 * c + 3]));
+  if constexpr (NC == 128)
+    tmem_st32(p_addr, w);
+  else
+    tmem_st16(p_addr, *reinterpret_cast<uint32_t(*)[16]>(&w[0]));
 }
 // One key pair (or a single trailing block, NC = 64) for one query row of one
 // tile.  The second block's scores load from TMEM while the first block's
 // maximum is taken.  The running max m moves (to the tile max) only when the
 // tile max exceeds it by more than kTau; then O is rescaled.  cnt = steps this
-// tile already processed: the PV of step cnt - 1 may still be running and is
-// waited for, on pv_done, only before O is rescaled.  P is double-buffered: the
-// buffer written here was last read by the PV of step cnt - 2, which the MMA
-// warp issued before this step's S, so it completed before S did.
+// tile already processed.  The MMA warp issued the PV of step cnt - 1 before
+// this step's S, so that PV (the last reader of the P columns and the last
+// writer of O) completed before S did: no MMA of this tile runs while the step
+// rescales O or writes P.
 template <int NC, int KG>
-__device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint8_t* prow, int r,
+__device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, uint32_t p_addr,
                                              const float (&c0)[KG], const float (&c1)[KG], int n0, int n1, int cnt,
-                                             float& m, float& l, uint64_t* pv_done, volatile int* abort_flag) {
+                                             float& m, float& l) {
   uint32_t s[128];
   __syncwarp();
   tmem_ld32(s_addr, H3B_S32(s, 0));
@@ -380,8 +378,7 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
     alpha = ex2(m - m_new);
     m = m_new;
     if (cnt > 0) {
-      if (!mbar_wait_warp(pv_done, (uint32_t)((cnt - 1) & 1), abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
-      tc_fence_after();
+      // the PV of the previous step completed before this step's S (issued after it)
       __syncwarp();
 #pragma unroll 1
       for (int c = 0; c < 128; c += 16) {
@@ -405,9 +402,8 @@ __device__ __forceinline__ bool softmax_step(uint32_t s_addr, uint32_t o_addr, u
     for (int g = 0; g < KG; ++g) o1[g] = off - kMagicF * c1[g];
     psum += exp_block<64, KG>(s, c1, o1);
   }
-  store_p<NC>(s, prow, r);
+  store_p<NC>(s, p_addr);
   tmem_wait_st();
-  fence_proxy_async_smem();
   tc_fence_before();
   l = l * alpha + psum;
   return true;
@@ -425,8 +421,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* kv_full = bars + 1;              // kKVStages
   uint64_t* kv_empty = kv_full + kKVStages;  // kKVStages
   uint64_t* s_full = kv_empty + kKVStages;   // 2 (per tile): S MMA done
-  uint64_t* pv_done = s_full + 2;            // 2 (per tile): PV MMA done
-  uint64_t* p_full = pv_done + 2;            // 2 (per tile, 128 arrivals): P written, S read
+  uint64_t* p_full = s_full + 2;             // 2 (per tile, 128 arrivals): P written, S read
   uint64_t* o_full = p_full + 2;             // 2 (per tile)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -445,7 +440,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&pv_done[t], 1);
       mbar_init(&p_full[t], kTileThreads);
     }
     mbar_init(&o_full[0], 1);
@@ -513,7 +507,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // MMA issuer of tile t = warp - 2: the whole warp runs the CTA's step
     // schedule (so the descriptors live in uniform registers), one elected lane
     // issues tcgen05.mma / commit.  At each step of its tile: [wait P of the
-    // tile's previous step] S(this step), PV(previous step).  Every stage takes
+    // tile's previous step] PV(previous step), S(this step).  Every stage takes
     // one release per tile per fill (kv_empty counts 2): a commit after the
     // tile's PV on it, or a plain arrive at the steps the tile skips.
     const int t = warp - 2;
@@ -522,17 +516,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool ok = mbar_wait_warp(q_full, 0, abort_flag, H3B_STATUS_ATTN_TIMEOUT);
     constexpr uint32_t idesc_pv = idesc_e4m3(128, 128);
     const uint64_t qdesc = sdesc_kmajor_sw128(smem_u32(smem + kOffQ + t * kQBytes));
-    const uint32_t pbase0 = smem_u32(smem + kOffP + 2 * t * kPBytes);  // P buffer of this tile's even steps
     const uint32_t kv_addr = smem_u32(smem + kOffKV);
     const uint64_t bias_a = sdesc_core_repeat(smem_u32(smem + kOffBias));
     const uint64_t bias_b = sdesc_core_repeat(smem_u32(smem + kOffBias + 128));
     const uint32_t s_tmem = tmem + (uint32_t)(t * 128);
     const uint32_t o_tmem = tmem + 256 + (uint32_t)(t * 128);
+    const uint32_t p_tmem = s_tmem + 96;  // P over S columns 96..127 (the S row is in registers by then)
     int stage = 0;
     uint32_t phase = 0;
     int pst = -1;          // stage of the pending PV (-1: none)
     bool ptwo = false, first = true;
-    uint32_t pbuf = 0;     // P buffer of the pending PV
     uint32_t ppar = 0;     // parity of the next p_full phase
     auto wait_p = [&]() -> bool {
       if (!mbar_wait_warp(&p_full[t], ppar, abort_flag, H3B_STATUS_ATTN_TIMEOUT)) return false;
@@ -540,23 +533,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       return true;
     };
+    // PV of the pending step, A = P from tensor memory (32 keys = 8 columns per MMA)
     auto issue_pv = [&]() {
       const uint32_t vbase = kv_addr + (uint32_t)(pst * kKVBytes + 16384);
-      const uint32_t pbase = pbase0 + pbuf * (uint32_t)kPBytes;
       if (elect_one()) {
-        mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase), sdesc_kmajor_sw64(vbase), idesc_pv, first ? 0u : 1u);
-        mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 32), sdesc_kmajor_sw64(vbase + 32), idesc_pv, 1u);
+        mma_f8_ts(o_tmem, p_tmem, sdesc_kmajor_sw64(vbase), idesc_pv, first ? 0u : 1u);
+        mma_f8_ts(o_tmem, p_tmem + 8, sdesc_kmajor_sw64(vbase + 32), idesc_pv, 1u);
         if (ptwo) {
-          mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 64), sdesc_kmajor_sw64(vbase + 8192), idesc_pv, 1u);
-          mma_f8_ss(o_tmem, sdesc_kmajor_sw128(pbase + 96), sdesc_kmajor_sw64(vbase + 8192 + 32), idesc_pv, 1u);
+          mma_f8_ts(o_tmem, p_tmem + 16, sdesc_kmajor_sw64(vbase + 8192), idesc_pv, 1u);
+          mma_f8_ts(o_tmem, p_tmem + 24, sdesc_kmajor_sw64(vbase + 8192 + 32), idesc_pv, 1u);
         }
-        mma_commit(&pv_done[t]);
         mma_commit(&kv_empty[pst]);
       }
       __syncwarp();
       first = false;
       pst = -1;
-      pbuf ^= 1u;
     };
     int j0, j1, who;
     while (ok && it.next(j0, j1, who)) {
@@ -564,8 +555,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       if ((who >> t) & 1) {
         const bool two = j1 >= 0;
-        // S of this step reuses the S columns: the previous P must be written
-        if (pst >= 0 && !wait_p()) { ok = false; break; }
+        // the previous step's PV first: its P lies in the S columns this step's S
+        // overwrites (MMAs of one thread run in issue order)
+        if (pst >= 0) {
+          if (!wait_p()) { ok = false; break; }
+          issue_pv();
+        }
         const uint64_t kdesc = sdesc_kmajor_sw128(kv_addr + (uint32_t)(stage * kKVBytes));
         const uint32_t idesc_s = two ? idesc_i8(128, 128) : idesc_i8(128, 64);
         if (elect_one()) {
@@ -575,7 +570,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mma_commit(&s_full[t]);
         }
         __syncwarp();
-        if (pst >= 0) issue_pv();
         pst = stage;
         ptwo = two;
         if (!it.pending(t)) {
@@ -608,7 +602,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + (uint32_t)(t * 128);
     const uint32_t o_addr = tmem + lane_off + 256 + (uint32_t)(t * 128);
-    uint8_t* prow0 = smem + kOffP + 2 * t * kPBytes + r * 128;
+    const uint32_t p_addr = s_addr + 96;
     const float* ksc = a.k_scale + (int64_t)h * a.Kb * KG;
     TileStream ts;
     ts.init(a, h, qta + t, t == 0 || has_b);
@@ -644,11 +638,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       tc_fence_after();
-      uint8_t* prow = prow0 + (cnt & 1) * kPBytes;
-      ok = two ? softmax_step<128, KG>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
-                                       abort_flag)
-               : softmax_step<64, KG>(s_addr, o_addr, prow, r, c0, c1, n0, n1, cnt, m, l, &pv_done[t],
-                                      abort_flag);
+      ok = two ? softmax_step<128, KG>(s_addr, o_addr, p_addr, c0, c1, n0, n1, cnt, m, l)
+               : softmax_step<64, KG>(s_addr, o_addr, p_addr, c0, c1, n0, n1, cnt, m, l);
       if (!ok) break;
       mbar_arrive(&p_full[t]);
       ++cnt;
