@@ -33,6 +33,47 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(EXPORTED), "ctypes signature table and header disagree"
 
 
+def _header_declarations():
+    """name -> (return type, [parameter type]) for every entry point of include/h3b.h."""
+    text = open(os.path.join(ROOT, "include", "h3b.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = {}
+    for ret, name, params in re.findall(r"([A-Za-z_][\w ]*?\**)\s*\b(h3b_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text,
+                                        flags=re.S):
+        params = " ".join(params.split())
+        types = [] if params in ("", "void") else [p.strip().rsplit(" ", 1)[0] if "*" not in p.strip().rsplit(" ", 1)[-1]
+                                                   else p.strip() for p in params.split(",")]
+        decls[name] = (" ".join(ret.split()), types)
+    return decls
+
+
+def _category(c_type: str) -> str:
+    if "*" in c_type:
+        return "pointer"
+    return {"int64_t": "int64", "int": "int", "float": "float"}[c_type.replace("const ", "").strip()]
+
+
+def _ctypes_category(t) -> str:
+    if t is ctypes.c_void_p or (isinstance(t, type) and issubclass(t, ctypes._Pointer)):
+        return "pointer"
+    return {ctypes.c_int64: "int64", ctypes.c_int: "int", ctypes.c_float: "float"}[t]
+
+
+def test_ctypes_signatures_match_the_header_parameter_by_parameter():
+    from h3b._lib import _RESTYPES, _SIGNATURES
+
+    decls = _header_declarations()
+    assert set(decls) == set(_SIGNATURES)
+    for name, (ret, params) in decls.items():
+        restype = _RESTYPES.get(name, ctypes.c_int)
+        assert (ret, restype) in (("int", ctypes.c_int), ("int64_t", ctypes.c_int64),
+                                  ("const char*", ctypes.c_char_p)), f"{name} returns {ret}, ctypes {restype}"
+        argtypes = _SIGNATURES[name]
+        assert len(params) == len(argtypes), f"{name}: header has {len(params)} parameters, ctypes {len(argtypes)}"
+        for i, (c_type, t) in enumerate(zip(params, argtypes)):
+            assert _category(c_type) == _ctypes_category(t), f"{name} parameter {i}: {c_type} vs {t}"
+
+
 def test_version_and_error_string():
     assert lib().h3b_version().startswith(b"h3b")
     assert lib().h3b_last_error() is not None
