@@ -229,16 +229,6 @@ __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t adesc, uint6
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// D(tmem) (+)= A(smem desc) * B(smem desc)^T, fp8 x fp8 -> fp32
-__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // D(tmem) (+)= A(tmem) * B(smem desc)^T, fp8 x fp8 -> fp32; A row m in tensor-memory
 // lane m, four consecutive K elements per 32-bit column (the lowest in bits 0..7)
 __device__ __forceinline__ void mma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
